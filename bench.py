@@ -1,0 +1,357 @@
+"""Benchmark of the B200 paged decode attention (HELM's long-context decode hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload ("config 2"): isolated paged decode
+attention, bf16, batch 4, 32 query heads / 8 KV heads (GQA 4), head_dim 128,
+32768 tokens per sequence in 16-token pages placed by a seeded random
+permutation of a 16384-page pool (1 GiB of K/V), Q/K/V ~ N(0,1), no mask.
+A STEP is one decode-attention call over the whole batch; the K/V cache is
+resident state in HBM (as in decode), the per-step inputs are q, the page
+table and the lengths.  512 MiB of K/V are read per step, so every step
+streams more than the 126 MB L2 (no flush needed).
+
+Prints one JSON line (rank 0).  `value` is achieved algorithmic HBM GB/s over
+all ranks (bytes of K/V + q + O + LSE + page table per step / device time).
+With N GPUs (torchrun) every rank runs its own config-2 problem (the path
+shards by sequence and KV head with no exchange): weak scaling, time = max
+over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+METRIC = ("decode tok/s at 32k/128k ctx; paged-attn achieved HBM GB/s vs 8 TB/s peak")
+B, HQ, HKV, D, P, T, POOL = 4, 32, 8, 128, 16, 32768, 16384
+KV_BYTES = B * T * HKV * D * 2 * 2
+ALG_BYTES = KV_BYTES + B * HQ * D * 2 * 2 + B * HQ * 4 + B * (T // P) * 4 + B * 4
+WORKLOAD = ("config2: isolated paged decode attention, bf16, B=4, 32q/8kv heads, D=128, "
+            "T=32768/seq, 16-token pages, randperm placement in a 16384-page pool")
+
+
+def _set_shape(seq_len: int, pool_pages: int) -> None:
+    """Shrinks the workload for profiling runs; the defaults are config 2."""
+    global T, POOL, KV_BYTES, ALG_BYTES, WORKLOAD
+    if seq_len == T and pool_pages == POOL:
+        return
+    if seq_len % P or pool_pages < B * seq_len // P:
+        raise SystemExit("--seq-len must be a multiple of 16 and fit the pool")
+    T, POOL = seq_len, pool_pages
+    KV_BYTES = B * T * HKV * D * 2 * 2
+    ALG_BYTES = KV_BYTES + B * HQ * D * 2 * 2 + B * HQ * 4 + B * (T // P) * 4 + B * 4
+    WORKLOAD = WORKLOAD.replace("T=32768", f"T={T}").replace("16384-page", f"{POOL}-page") + \
+        " (reduced profiling case)"
+
+
+def _peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def make_inputs(seed: int = 0):
+    """Draw order: permutation, K pool, V pool, q (torch CPU generator, seed 0)."""
+    g = torch.Generator().manual_seed(seed)
+    perm = torch.randperm(POOL, generator=g)
+    k = torch.randn(POOL, HKV, P, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(POOL, HKV, P, D, generator=g).to(torch.bfloat16)
+    q = torch.randn(B, HQ, D, generator=g).to(torch.bfloat16)
+    pool = torch.stack([k, v], dim=1)  # [POOL, 2, HKV, P, D]
+    page_table = perm[:B * (T // P)].view(B, T // P).to(torch.int32)
+    kv_lens = torch.full((B,), T, dtype=torch.int32)
+    return q, pool, page_table, kv_lens
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        with open(self.file.name) as f:
+            rows = [r.strip().split(", ") for r in f if r.strip()]
+        os.unlink(self.file.name)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except ValueError:
+                continue
+            for n, flag in zip(names, r[5:9]):
+                if flag.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def cpu_baseline(q, pool, page_table, kv_lens, budget_s: float = 12.0, steps: int | None = None):
+    """The oracle port (oracle/paged_attention.c) over the full config-2 workload,
+    all host threads; repeated until `budget_s` elapsed (or `steps` times)."""
+    import oracle
+    threads = os.cpu_count() or 1
+    nump, used = oracle.dense_page_lists(kv_lens.numpy(), P, page_table.shape[1])
+    bits = pool.view(torch.int16).numpy().view(np.uint16)
+    qf = q.float().numpy()
+    pt = page_table.numpy()
+
+    def once():
+        return oracle.paged_attention(qf, bits, oracle.DT_BF16, pt, nump, used,
+                                      num_kv_heads=HKV, page_size=P, scale=D ** -0.5,
+                                      threads=threads)
+    once()  # warm (page faults, thread start-up)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        once()
+        times.append(time.perf_counter() - t0)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() - t_start > budget_s:
+            break
+    per = statistics.median(times)
+    cpu = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    cpu = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"value": ALG_BYTES / per / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"full config-2 workload (4x32768 tokens, 512 MiB K/V) per call, "
+                      f"median of {len(times)} calls, {per * 1e3:.1f} ms/call, CPU: {cpu}",
+            "times": times}
+
+
+def run_reference(args, rank: int):
+    if rank != 0:
+        return
+    q, pool, pt, kl = make_inputs(0)
+    for _ in range(args.warmup):
+        cpu_baseline(q, pool, pt, kl, steps=1)
+    res = cpu_baseline(q, pool, pt, kl, steps=args.steps)
+    per = sum(res["times"]) / len(res["times"])
+    line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "parallelism": "host threads"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args, rank: int, world: int, dev: torch.device):
+    from helm_b200 import _capi
+    q, pool, pt, kl = make_inputs(0)
+    qd, pd, ptd, kld = q.to(dev), pool.to(dev), pt.to(dev), kl.to(dev)
+    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, HQ, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        _capi.paged_decode_attention(qd, pd, ptd, kld, num_kv_heads=HKV, page_size=P,
+                                     scale=D ** -0.5, out=out, lse=lse, max_kv_len_hint=T)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    if _capi.device_status(dev) != 0:
+        raise RuntimeError("device status reported an error during warm-up")
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    # ---- device-resident timing (value) --------------------------------------
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per_step_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                       for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index) as clocks:
+        # keep the GPU under the same load for ~0.6 s so that nvidia-smi sees it
+        t_soak = time.perf_counter()
+        while time.perf_counter() - t_soak < 0.6:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize(dev)
+        ev0.record(stream)
+        for i in range(args.steps):
+            per_step_events[i][0].record(stream)
+            step()
+            per_step_events[i][1].record(stream)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    elapsed_ms = ev0.elapsed_time(ev1)
+    step_ms = [a.elapsed_time(b) for a, b in per_step_events]
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    elapsed_ms = float(t.item())
+    value = ALG_BYTES * args.steps * world / (elapsed_ms / 1e3) / 1e9
+
+    # ---- end to end through the public API, host buffers ---------------------
+    q_host = q.clone().pin_memory()
+    pt_host = pt.clone().pin_memory()
+    kl_host = kl.clone().pin_memory()
+    out_host = torch.empty(B, HQ, D, dtype=torch.bfloat16).pin_memory()
+    lse_host = torch.empty(B, HQ, dtype=torch.float32).pin_memory()
+    h2d = q_host.numel() * 2 + pt_host.numel() * 4 + kl_host.numel() * 4
+    d2h = out_host.numel() * 2 + lse_host.numel() * 4
+
+    def e2e_step():
+        qd.copy_(q_host, non_blocking=True)
+        ptd.copy_(pt_host, non_blocking=True)
+        kld.copy_(kl_host, non_blocking=True)
+        step()
+        out_host.copy_(out, non_blocking=True)
+        lse_host.copy_(lse, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    t2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
+    e2e_value = ALG_BYTES * args.steps * world / (float(t2.item()) / 1e3) / 1e9
+    # the end-to-end result must equal the device-resident one
+    torch.cuda.synchronize(dev)
+    if not torch.equal(out_host.to(dev), out):
+        raise RuntimeError("end-to-end output differs from the device-resident output")
+
+    if rank != 0:
+        return
+    peak, peak_src = _peaks()
+    avg_launch_ms = statistics.mean(step_ms)
+    achieved = ALG_BYTES / (avg_launch_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(REPO, "profiles", "paged_decode_config2_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "kv_bytes_per_step": KV_BYTES,
+                   "algorithmic_bytes_per_step": ALG_BYTES,
+                   "l2": "inputs larger than L2 (512 MiB K/V streamed per step), no flush",
+                   "parallelism": f"replicas x{world} (shard by sequence/KV head, no exchange)",
+                   "decode_attention_calls_per_s": 1e3 / (elapsed_ms / args.steps) * world,
+                   "sequences_decoded_per_s_one_layer":
+                       B * 1e3 / (elapsed_ms / args.steps) * world},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "paged_decode_kernel (one launch per step; split-KV merge fused)",
+                     "peak_source": peak_src,
+                     "clock_note": "clocks sampled over a 0.6 s soak at the same load "
+                                   "immediately before and during the timed region"},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(q, pool, pt, kl)
+        line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seq-len", type=int, default=T,
+                    help="tokens per sequence (profiling a smaller case only)")
+    ap.add_argument("--pool-pages", type=int, default=POOL,
+                    help="page-pool slots (profiling a smaller case only)")
+    args = ap.parse_args()
+    _set_shape(args.seq_len, args.pool_pages)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                             device_id=dev)
+    try:
+        run_b200(args, rank, world, dev)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

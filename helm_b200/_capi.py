@@ -1,0 +1,324 @@
+"""ctypes binding of libhelm_b200.so (the C ABI declared in include/helm_b200.h)
+plus thin wrappers that take torch tensors and pass their raw pointers.
+
+PyTorch is only the plumbing here: it owns device memory and streams.  Every
+computation runs in the native library; when the library is missing these
+functions raise instead of computing anything another way.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+import torch
+
+from . import build as _build
+
+HELM_OK = 0
+DTYPE_FP32, DTYPE_FP16, DTYPE_BF16 = 0, 1, 2
+DEV_TIMEOUT, DEV_BAD_PAGE = 1, 2
+
+_TORCH_TO_HELM = {torch.float32: DTYPE_FP32, torch.float16: DTYPE_FP16,
+                  torch.bfloat16: DTYPE_BF16}
+
+# name -> (restype, argtypes); must match include/helm_b200.h exactly.
+_P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+_SIGNATURES = {
+    "helm_version": (_I, []),
+    "helm_status_string": (ctypes.c_char_p, [_I]),
+    "helm_last_cuda_error": (ctypes.c_char_p, []),
+    "helm_get_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I, _P]),
+    "helm_paged_decode_workspace_bytes": (_I64, [_I, _I, _I, _I]),
+    "helm_paged_decode_attention": (_I, [
+        _P, _I64, _I64,            # q, strides
+        _P, _I64,                  # pool, pool_pages
+        _P, _I64, _I,              # page_table, pt_stride_b, max_pages
+        _P, _P, _P, _P,            # kv_lens, num_pages, page_used, page_start
+        _P, _I, _I64,              # mask, mask_dtype, mask_stride_b
+        _P, _I64, _I64, _P,        # out, strides, lse
+        _P, _I64,                  # workspace, bytes
+        _I, _I, _I, _I, _I, _I,    # batch, hq, hkv, head_dim, page_size, dtype
+        _F, _F, _I, _P]),          # scale, softcap, max_kv_len_hint, stream
+    "helm_kv_append": (_I, [
+        _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,   # q, k, v
+        _P, _P, _F,                                       # norm weights, eps
+        _P, _P, _I64,                                     # cos, sin, stride
+        _P, _I64, _I64, _P, _P,                           # q_out, k_out, v_out
+        _P, _I64, _P,                                     # pool, pool_pages, slot_rows
+        _I, _I, _I, _I, _I, _I, _P]),
+    "helm_copy_pages": (_I, [_P, _P, _I64, _P, _P, _I64, _P]),
+    "helm_gather_kv": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "helm_merge_attention_states": (_I, [_P, _I, _P, _I, _I64, _I, _P, _I, _P, _P]),
+}
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+class HelmError(RuntimeError):
+    """A helm_b200 C-ABI call returned a non-zero status."""
+
+
+def library_path() -> str:
+    return _build.LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libhelm_b200.so (building it first if its sources changed and
+    nvcc is available).  Raises if the library cannot be loaded."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lib_lock:
+        if _lib is None:
+            path = _build.LIB_PATH
+            if _build.needs_build():
+                try:
+                    _build.build()
+                except Exception as exc:  # noqa: BLE001 - re-raised below with context
+                    if not os.path.exists(path):
+                        raise HelmError(f"helm_b200 native library is not built and the build "
+                                        f"failed: {exc}") from exc
+            if not os.path.exists(path):
+                raise HelmError(f"helm_b200 native library not found at {path}; "
+                                f"run `python -m helm_b200.build`")
+            handle = ctypes.CDLL(path)
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != HELM_OK:
+        L = lib()
+        msg = L.helm_status_string(rc).decode()
+        cuda = L.helm_last_cuda_error().decode()
+        raise HelmError(f"{what}: {msg}" + (f" ({cuda})" if cuda and rc == 3 else ""))
+
+
+def helm_dtype(dt: torch.dtype) -> int:
+    try:
+        return _TORCH_TO_HELM[dt]
+    except KeyError:
+        raise HelmError(f"unsupported dtype {dt}") from None
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device, stream=None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    return s.cuda_stream
+
+
+def device_status(device: torch.device, reset: bool = True, stream=None) -> int:
+    """Synchronises `stream` and returns the device status word (HELM_DEV_* bits).
+    A non-zero word also re-zeroes the decode workspace counters, which an
+    abandoned call may have left set."""
+    out = ctypes.c_uint(0)
+    with torch.cuda.device(device):
+        _check(lib().helm_get_device_status(ctypes.byref(out), int(reset),
+                                            _stream_handle(device, stream)),
+               "helm_get_device_status")
+    if out.value:
+        reset_workspace(device)
+    return out.value
+
+
+# ------------------------------------------------------------------ workspace --
+class _Workspace:
+    """Per-device scratch of the decode kernel: per-pair counters (must be zero
+    at call start; a completed call leaves them zero) then fp32 partials."""
+
+    def __init__(self):
+        self.buf: Optional[torch.Tensor] = None
+        self.clean_counter_bytes = 0   # prefix known to be zero
+
+    def get(self, device: torch.device, nbytes: int, counter_bytes: int) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() < nbytes:
+            self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            self.clean_counter_bytes = self.buf.numel()
+        if counter_bytes > self.clean_counter_bytes:
+            self.buf[:counter_bytes].zero_()
+        # partials of this call start right after its counters
+        self.clean_counter_bytes = counter_bytes
+        return self.buf
+
+
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int, counter_bytes: int) -> torch.Tensor:
+    key = (device.type, device.index)
+    ws = _workspaces.get(key)
+    if ws is None:
+        ws = _workspaces[key] = _Workspace()
+    return ws.get(device, nbytes, counter_bytes)
+
+
+def reset_workspace(device: torch.device) -> None:
+    """Re-zeroes the counters, e.g. after a call that reported an error."""
+    ws = _workspaces.get((device.type, device.index))
+    if ws is not None and ws.buf is not None:
+        ws.buf.zero_()
+        ws.clean_counter_bytes = ws.buf.numel()
+
+
+def decode_workspace_bytes(device: torch.device, batch: int, hq: int, hkv: int, d: int) -> int:
+    with torch.cuda.device(device):
+        return int(lib().helm_paged_decode_workspace_bytes(batch, hq, hkv, d))
+
+
+# ------------------------------------------------------------------- wrappers --
+def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor,
+                           kv_lens: torch.Tensor, *, num_kv_heads: int, page_size: int,
+                           scale: float, softcap: Optional[float] = None,
+                           mask: Optional[torch.Tensor] = None,
+                           num_pages: Optional[torch.Tensor] = None,
+                           page_used: Optional[torch.Tensor] = None,
+                           page_start: Optional[torch.Tensor] = None,
+                           out: Optional[torch.Tensor] = None,
+                           lse: Optional[torch.Tensor] = None,
+                           max_kv_len_hint: int = 0, stream=None):
+    """Decode attention over a page pool.
+
+    q [B, Hq, D] (dim stride 1); pool [slots, 2, Hkv, P, D]; page_table int32
+    [B, max_pages]; kv_lens int32 [B]; mask additive [B, T] (or None).
+    Returns (out [B, Hq, D] in q.dtype, lse fp32 [B, Hq] or None).
+    """
+    if q.device.type != "cuda":
+        raise HelmError("paged_decode_attention runs on CUDA tensors only")
+    B, Hq, D = q.shape
+    if q.stride(2) != 1:
+        raise HelmError("q must have a unit stride on the head dim")
+    if pool.dtype != q.dtype:
+        raise HelmError(f"KV pool dtype {pool.dtype} != query dtype {q.dtype}")
+    if page_table.dtype != torch.int32 or kv_lens.dtype != torch.int32:
+        raise HelmError("page_table and kv_lens must be int32")
+    if page_table.stride(1) != 1:
+        raise HelmError("page_table rows must be contiguous")
+    dev = q.device
+    if out is None:
+        out = torch.empty(B, Hq, D, dtype=q.dtype, device=dev)
+    ws_bytes = decode_workspace_bytes(dev, B, Hq, num_kv_heads, D)
+    ws = _workspace(dev, ws_bytes, ((4 * B * num_kv_heads + 255) // 256) * 256)
+    mask_ptr, mask_dt, mask_sb = None, 0, 0
+    if mask is not None:
+        if mask.stride(-1) != 1:
+            mask = mask.contiguous()
+        mask_ptr, mask_dt = mask.data_ptr(), helm_dtype(mask.dtype)
+        mask_sb = mask.stride(0) if mask.shape[0] > 1 else 0
+    with torch.cuda.device(dev):
+        rc = lib().helm_paged_decode_attention(
+            q.data_ptr(), q.stride(0), q.stride(1),
+            pool.data_ptr(), pool.shape[0],
+            page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+            kv_lens.data_ptr(), _ptr(num_pages), _ptr(page_used), _ptr(page_start),
+            mask_ptr, mask_dt, mask_sb,
+            out.data_ptr(), out.stride(0), out.stride(1), _ptr(lse),
+            ws.data_ptr(), ws.numel(),
+            B, Hq, num_kv_heads, D, page_size, helm_dtype(q.dtype),
+            float(scale), float(softcap or 0.0), int(max_kv_len_hint),
+            _stream_handle(dev, stream))
+    _check(rc, "helm_paged_decode_attention")
+    return out, lse
+
+
+def kv_append(*, k: torch.Tensor, v: torch.Tensor, pool: Optional[torch.Tensor],
+              slot_rows: Optional[torch.Tensor], page_size: int,
+              q: Optional[torch.Tensor] = None, q_out: Optional[torch.Tensor] = None,
+              q_norm_w: Optional[torch.Tensor] = None, k_norm_w: Optional[torch.Tensor] = None,
+              eps: float = 1e-6, cos: Optional[torch.Tensor] = None,
+              sin: Optional[torch.Tensor] = None, k_out: Optional[torch.Tensor] = None,
+              v_out: Optional[torch.Tensor] = None, stream=None) -> None:
+    """Fused (QK-RMSNorm, RoPE, page write).  Token-major views:
+    q [N, Hq, D], k/v [N, Hkv, D] (unit dim stride), cos/sin [N, D],
+    slot_rows int64 [N] (pool row = slot*page_size + row, -1 = skip)."""
+    N, Hkv, D = k.shape
+    Hq = q.shape[1] if q is not None else 0
+    dev = k.device
+    for name, t in (("k", k), ("v", v), ("q", q), ("q_out", q_out)):
+        if t is not None and t.stride(-1) != 1:
+            raise HelmError(f"{name} must have a unit stride on the head dim")
+    if cos is not None and cos.stride(-1) != 1:
+        raise HelmError("cos/sin must have a unit stride on the head dim")
+    if slot_rows is not None and slot_rows.dtype != torch.int64:
+        raise HelmError("slot_rows must be int64")
+    with torch.cuda.device(dev):
+        rc = lib().helm_kv_append(
+            _ptr(q), q.stride(0) if q is not None else 0, q.stride(1) if q is not None else 0,
+            k.data_ptr(), k.stride(0), k.stride(1),
+            v.data_ptr(), v.stride(0), v.stride(1),
+            _ptr(q_norm_w), _ptr(k_norm_w), float(eps),
+            _ptr(cos), _ptr(sin), cos.stride(0) if cos is not None else 0,
+            _ptr(q_out), q_out.stride(0) if q_out is not None else 0,
+            q_out.stride(1) if q_out is not None else 0,
+            _ptr(k_out), _ptr(v_out),
+            _ptr(pool), pool.shape[0] if pool is not None else 0, _ptr(slot_rows),
+            N, Hq, Hkv, D, page_size, helm_dtype(k.dtype), _stream_handle(dev, stream))
+    _check(rc, "helm_kv_append")
+
+
+def copy_pages(dst_pool: torch.Tensor, src_pool: torch.Tensor, dst_slots, src_slots,
+               device: torch.device, stream=None) -> None:
+    """dst_pool[dst_slots[i]] = src_pool[src_slots[i]] on `stream` (copy engine)."""
+    n = len(dst_slots)
+    if n != len(src_slots):
+        raise HelmError("slot lists differ in length")
+    if n == 0:
+        return
+    page_bytes = dst_pool[0].numel() * dst_pool.element_size()
+    if src_pool[0].numel() * src_pool.element_size() != page_bytes:
+        raise HelmError("page size differs between pools")
+    dst = (ctypes.c_int64 * n)(*dst_slots)
+    src = (ctypes.c_int64 * n)(*src_slots)
+    with torch.cuda.device(device):
+        rc = lib().helm_copy_pages(dst_pool.data_ptr(), src_pool.data_ptr(), page_bytes,
+                                   dst, src, n, _stream_handle(device, stream))
+    _check(rc, "helm_copy_pages")
+
+
+def gather_kv(pool: torch.Tensor, page_table: torch.Tensor, kv_lens: torch.Tensor, t_max: int,
+              *, num_kv_heads: int, page_size: int, stream=None):
+    """Dense K, V [B, Hkv, t_max, D] from the page pool (zero beyond kv_lens)."""
+    B = page_table.shape[0]
+    D = pool.shape[-1]
+    dev = pool.device
+    k = torch.empty(B, num_kv_heads, t_max, D, dtype=pool.dtype, device=dev)
+    v = torch.empty_like(k)
+    with torch.cuda.device(dev):
+        rc = lib().helm_gather_kv(pool.data_ptr(), pool.shape[0], page_table.data_ptr(),
+                                  page_table.stride(0), page_table.shape[1], kv_lens.data_ptr(),
+                                  k.data_ptr(), v.data_ptr(), B, num_kv_heads, D, page_size,
+                                  t_max, helm_dtype(pool.dtype), _stream_handle(dev, stream))
+    _check(rc, "helm_gather_kv")
+    return k, v
+
+
+def merge_attention_states(o_parts: torch.Tensor, lse_parts: torch.Tensor,
+                           out_dtype: torch.dtype, stream=None):
+    """o_parts [R, ..., D], lse_parts fp32 [R, ...] -> (out [..., D], lse fp32 [...])."""
+    R = o_parts.shape[0]
+    D = o_parts.shape[-1]
+    rows = lse_parts[0].numel()
+    o_parts = o_parts.contiguous()
+    lse_parts = lse_parts.contiguous().float()
+    dev = o_parts.device
+    out = torch.empty(o_parts.shape[1:], dtype=out_dtype, device=dev)
+    lse = torch.empty(lse_parts.shape[1:], dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib().helm_merge_attention_states(
+            o_parts.data_ptr(), helm_dtype(o_parts.dtype), lse_parts.data_ptr(), R, rows, D,
+            out.data_ptr(), helm_dtype(out_dtype), lse.data_ptr(), _stream_handle(dev, stream))
+    _check(rc, "helm_merge_attention_states")
+    return out, lse

@@ -1,0 +1,823 @@
+// Paged decode attention for sm_100a (B200).
+//
+// Replaces the per-page eager loop / torch.cat+SDPA of HELM's
+// perform_streaming_attention (helm/runtime/kv_cache.py:405-662) and the paged
+// branches of _decode_batched (helm/runtime/kv_offload.py:144-186) with one
+// persistent kernel launch.
+//
+// Work unit: a TILE = 16 consecutive token rows of one page of one KV head
+// (K: 16 x D, V: 16 x D).  All tiles of all (sequence, kv-head) PAIRS are laid
+// out in one flattened order (sequence-major, then kv head, then tile) and cut
+// into equal contiguous ranges, one per WORKER (a consumer warp).  A worker
+// walks its range, keeps an online-softmax state for the G query heads of the
+// current pair, and when its range leaves a pair either writes the final
+// output (it covered the whole pair) or an fp32 partial state (m, l,
+// unnormalised O) at the unique slot worker + pair.  After its loop, a CTA
+// bumps a per-pair counter for every split pair it touched; the CTA that
+// completes the count merges that pair's partials with all its consumer
+// warps and resets the counter (no second kernel, no spin-wait).
+//
+// Per CTA: one producer warp issues TMA tile loads (two 64-column boxes per K
+// or V tile, 128-byte swizzled so ldmatrix reads are bank-conflict free) into
+// a ring of NS stages; stage s holds tile s of each of the CTA's NCW workers.
+// Full/empty mbarriers hand stages between producer and consumers.
+//
+// Math per tile (tensor cores, mma.sync m16n8k16, fp32 accumulate):
+//   S^T[16 tok x 8 heads] = K[16 x D] . Q^T[D x 8]        (tokens fill M)
+//   online softmax over tokens per head (warp shuffles, exp2 domain)
+//   O^T[D x 8] += V^T[D x 16] . P^T[16 x 8]               (P^T via movmatrix)
+// The GQA group (G <= 16 query heads per KV head) is the N dimension.
+#include "common.cuh"
+
+namespace helm {
+
+namespace {
+
+constexpr int kTileRows = 16;
+constexpr int kMaxNCW = 8;                   // most consumer warps (= workers) per CTA
+constexpr int kStageBudget = 196608;         // bytes of tile ring per CTA
+constexpr int kMaxBatch = 2048;              // prefix table held in shared memory
+constexpr int kMinTilesPerWorker = 8;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct DecodeArgs {
+  const void* q;
+  int64_t q_sb, q_sh;
+  int64_t pool_pages;
+  const int32_t* page_table;
+  int64_t pt_sb;
+  int max_pages;
+  const int32_t* kv_lens;
+  const int32_t* num_pages;   // ragged page lists (nullable, with the next two)
+  const int32_t* page_used;
+  const int32_t* page_start;
+  const void* mask;
+  int mask_dtype;
+  int64_t mask_sb;
+  void* out;
+  int64_t out_sb, out_sh;
+  float* lse;
+  float* part_o;    // [slots][G][D]
+  float* part_ml;   // [slots][G][2]  (m in log2 units, l)
+  int* counters;    // [B * Hkv] CTAs done per pair; zero between calls
+  int batch, hq, hkv, group, page_size, tiles_per_page;
+  float scale;
+  float scale_log2;
+  float softcap;
+  int num_workers;
+};
+
+__device__ __forceinline__ int div_up(int a, int b) { return (a + b - 1) / b; }
+
+// Number of tiles of every pair of sequence b.  Out-of-range page counts are
+// clamped (and reported) so that no page-table read leaves its row.
+__device__ __forceinline__ int tiles_of_seq(const DecodeArgs& a, int b) {
+  int n;
+  if (a.num_pages != nullptr) {
+    n = a.num_pages[b];
+  } else {
+    const int len = a.kv_lens[b];
+    n = len > 0 ? div_up(len, a.page_size) : 0;
+  }
+  if (n < 0) n = 0;
+  if (n > a.max_pages) {
+    report_status(HELM_DEV_BAD_PAGE);
+    n = a.max_pages;
+  }
+  return n * a.tiles_per_page;
+}
+
+// Fills s_cum[0..B] with the prefix sum of tiles per sequence (one warp).
+__device__ void build_prefix(const DecodeArgs& a, int* s_cum, int lane) {
+  int carry = 0;
+  if (lane == 0) s_cum[0] = 0;
+  for (int base = 0; base < a.batch; base += 32) {
+    const int b = base + lane;
+    int v = b < a.batch ? tiles_of_seq(a, b) : 0;
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, off);
+      if (lane >= off) v += n;
+    }
+    if (b < a.batch) s_cum[b + 1] = carry + v;
+    carry += __shfl_sync(0xffffffffu, v, 31);
+  }
+}
+
+struct TilePos {
+  int b, h, t;  // sequence, kv head, tile within the pair
+};
+
+// Maps a flattened tile index x (< total) to its (sequence, head, tile).
+__device__ __forceinline__ TilePos locate(const int* s_cum, int batch, int hkv, int x) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {  // largest b with s_cum[b] * hkv <= x
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_cum[mid] * hkv <= x)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const int tb = s_cum[lo + 1] - s_cum[lo];
+  const int r = x - s_cum[lo] * hkv;
+  TilePos p;
+  p.b = lo;
+  p.h = r / tb;
+  p.t = r - p.h * tb;
+  return p;
+}
+
+__device__ __forceinline__ void advance(TilePos& p, const int* s_cum, int batch, int hkv) {
+  const int tb = s_cum[p.b + 1] - s_cum[p.b];
+  if (++p.t < tb) return;
+  p.t = 0;
+  if (++p.h < hkv) return;
+  p.h = 0;
+  do {
+    ++p.b;
+  } while (p.b < batch && s_cum[p.b + 1] == s_cum[p.b]);
+}
+
+template <typename T>
+__device__ __forceinline__ float load_mask(const DecodeArgs& a, int b, int tok) {
+  const int64_t off = static_cast<int64_t>(b) * a.mask_sb + tok;
+  if (a.mask_dtype == HELM_DTYPE_FP32) return static_cast<const float*>(a.mask)[off];
+  if (a.mask_dtype == HELM_DTYPE_BF16)
+    return __bfloat162float(static_cast<const __nv_bfloat16*>(a.mask)[off]);
+  return __half2float(static_cast<const __half*>(a.mask)[off]);
+}
+
+// Additive mask value in log2 units.  A finite mask (e.g. finfo(float32).min)
+// stays finite instead of overflowing to -inf, so a row whose every key is
+// masked with a finite value behaves as in eager fp32 arithmetic.
+__device__ __forceinline__ float mask_log2(float m) {
+  return m == -INFINITY ? -INFINITY : fmaxf(m * kLog2e, -3.0e38f);
+}
+
+template <typename T, int D, int NT>
+struct Worker {
+  static constexpr int KS = D / 16;  // k-steps over the head dim, = m-tiles of O^T
+  float m[NT][2];
+  float l[NT][2];
+  float o[NT][KS][4];
+  uint32_t qf[NT][KS][2];
+  int cur_b = -1, cur_h = -1;
+
+  __device__ __forceinline__ void reset() {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        m[nt][j] = -INFINITY;
+        l[nt][j] = 0.f;
+      }
+#pragma unroll
+      for (int mt = 0; mt < KS; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[nt][mt][e] = 0.f;
+    }
+  }
+
+  __device__ __forceinline__ void load_q(const DecodeArgs& a, int b, int h, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const T* qb = static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_sb;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int hg = nt * 8 + g;
+      const bool ok = hg < a.group;
+      const T* qh = qb + static_cast<int64_t>(h * a.group + (ok ? hg : 0)) * a.q_sh;
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        const uint32_t w0 = ok ? *reinterpret_cast<const uint32_t*>(qh + kk * 16 + 2 * t) : 0u;
+        const uint32_t w1 =
+            ok ? *reinterpret_cast<const uint32_t*>(qh + kk * 16 + 8 + 2 * t) : 0u;
+        qf[nt][kk][0] = w0;
+        qf[nt][kk][1] = w1;
+      }
+    }
+  }
+
+  // Ends the current pair: when this worker covered the whole pair it writes
+  // the normalised output and LSE; otherwise its partial state goes to slot
+  // worker + pair for the merge.
+  __device__ __forceinline__ void flush(const DecodeArgs& a, const int* s_cum, int W, int v,
+                                        int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    const int b = cur_b, h = cur_h, p = b * a.hkv + h;
+    const int tb = s_cum[b + 1] - s_cum[b];
+    const int st = s_cum[b] * a.hkv + h * tb;
+    const bool alone = (st / W) == ((st + tb - 1) / W);
+    T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float lt = warp_sum_xor(l[nt][j], 4, 16);
+        const int hg = nt * 8 + 2 * t + j;
+        if (hg >= a.group) continue;
+        if (alone) {
+          const float inv = 1.f / fmaxf(lt, 1e-12f);
+          T* oh = out + static_cast<int64_t>(h * a.group + hg) * a.out_sh;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            oh[mt * 16 + g] = from_float<T>(o[nt][mt][j] * inv);
+            oh[mt * 16 + 8 + g] = from_float<T>(o[nt][mt][2 + j] * inv);
+          }
+          if (g == 0 && a.lse != nullptr)
+            a.lse[static_cast<int64_t>(b) * a.hq + h * a.group + hg] =
+                (m[nt][j] == -INFINITY || lt <= 0.f) ? -INFINITY : m[nt][j] * kLn2 + logf(lt);
+        } else {
+          const int64_t slot = static_cast<int64_t>(v + p) * a.group + hg;
+          float* po = a.part_o + slot * D;
+#pragma unroll
+          for (int mt = 0; mt < KS; ++mt) {
+            po[mt * 16 + g] = o[nt][mt][j];
+            po[mt * 16 + 8 + g] = o[nt][mt][2 + j];
+          }
+          if (g == 0)
+            *reinterpret_cast<float2*>(a.part_ml + slot * 2) = make_float2(m[nt][j], lt);
+        }
+      }
+    }
+  }
+
+  __device__ __forceinline__ void tile(const DecodeArgs& a, uint32_t kbase, uint32_t vbase,
+                                       int valid, int tok0, int b, int lane) {
+    const int g = lane >> 2, t = lane & 3, mi = lane >> 3, r7 = lane & 7;
+    // ---- S^T = K . Q^T, two independent accumulation chains -----------------
+    float s[NT][4], s2[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[nt][e] = s2[nt][e] = 0.f;
+    {
+      const int r = r7 + ((mi & 1) << 3);
+#pragma unroll
+      for (int kk = 0; kk < KS; ++kk) {
+        const int c = ((kk & 3) << 1) + (mi >> 1);
+        const uint32_t addr = kbase + (kk >> 2) * 2048 + r * 128 + ((c ^ r7) << 4);
+        uint32_t af[4];
+        ldsm_x4(addr, af[0], af[1], af[2], af[3]);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (kk & 1)
+            MmaOp<T>::run(s2[nt], af, qf[nt][kk][0], qf[nt][kk][1]);
+          else
+            MmaOp<T>::run(s[nt], af, qf[nt][kk][0], qf[nt][kk][1]);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[nt][e] += s2[nt][e];
+    }
+    // ---- online softmax (log2 domain) ---------------------------------------
+    const bool v0 = g < valid, v1 = g + 8 < valid;
+    float madd0 = 0.f, madd1 = 0.f;
+    if (a.mask != nullptr) {
+      if (v0) madd0 = mask_log2(load_mask<T>(a, b, tok0 + g));
+      if (v1) madd1 = mask_log2(load_mask<T>(a, b, tok0 + g + 8));
+    }
+    uint32_t pb0[NT], pb1[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float p[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        float x0 = s[nt][j], x1 = s[nt][2 + j];
+        if (a.softcap > 0.f) {
+          x0 = a.softcap * tanhf(x0 * a.scale / a.softcap) * kLog2e;
+          x1 = a.softcap * tanhf(x1 * a.scale / a.softcap) * kLog2e;
+        } else {
+          x0 *= a.scale_log2;
+          x1 *= a.scale_log2;
+        }
+        x0 = v0 ? x0 + madd0 : -INFINITY;
+        x1 = v1 ? x1 + madd1 : -INFINITY;
+        const float mx = warp_max_xor(fmaxf(x0, x1), 4, 16);
+        const float m_new = fmaxf(m[nt][j], mx);
+        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+        const float alpha = exp2f(m[nt][j] - m_use);
+        const float p0 = exp2f(x0 - m_use), p1 = exp2f(x1 - m_use);
+        l[nt][j] = l[nt][j] * alpha + p0 + p1;
+        m[nt][j] = m_new;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+          o[nt][mt][j] *= alpha;
+          o[nt][mt][2 + j] *= alpha;
+        }
+        p[j] = p0;
+        p[2 + j] = p1;
+      }
+      pb0[nt] = movmatrix_trans(MmaOp<T>::pack(p[0], p[1]));
+      pb1[nt] = movmatrix_trans(MmaOp<T>::pack(p[2], p[3]));
+    }
+    // ---- O^T += V^T . P^T ----------------------------------------------------
+    uint32_t keep01 = 0xffffffffu, keep23 = 0xffffffffu;
+    if (valid < kTileRows) {
+      keep01 = (2 * t < valid ? 0x0000ffffu : 0u) | (2 * t + 1 < valid ? 0xffff0000u : 0u);
+      keep23 = (2 * t + 8 < valid ? 0x0000ffffu : 0u) | (2 * t + 9 < valid ? 0xffff0000u : 0u);
+    }
+    const int r = r7 + ((mi >> 1) << 3);
+#pragma unroll
+    for (int mt = 0; mt < KS; ++mt) {
+      const int c = ((mt & 3) << 1) + (mi & 1);
+      const uint32_t addr = vbase + (mt >> 2) * 2048 + r * 128 + ((c ^ r7) << 4);
+      uint32_t af[4];
+      ldsm_x4_trans(addr, af[0], af[1], af[2], af[3]);
+      af[0] &= keep01;
+      af[1] &= keep01;
+      af[2] &= keep23;
+      af[3] &= keep23;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) MmaOp<T>::run(o[nt][mt], af, pb0[nt], pb1[nt]);
+    }
+  }
+};
+
+__device__ __forceinline__ void consumer_barrier(int threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
+// Merges the partial states of pair p (workers vf..vl) with the CTA's
+// consumer threads; `scratch` is the (now idle) tile ring.
+template <typename T, int D, int NCW>
+__device__ void merge_pair(const DecodeArgs& a, int p, int vf, int vl, uint8_t* scratch) {
+  constexpr int kConsumers = NCW * 32;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = a.group, nparts = vl - vf + 1;
+  const int b = p / a.hkv, h = p - b * a.hkv;
+  float* s_w = reinterpret_cast<float*>(scratch);       // [nparts][G] weights
+  float* s_inv = s_w + nparts * G;                        // [G]
+  float4* s_red =                                         // [kConsumers] group partial sums
+      reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(s_inv + 16) + 15) & ~uintptr_t(15));
+  // per head: M = max m_j, weights 2^(m_j - M), 1/L and LSE
+  for (int hg = warp; hg < G; hg += NCW) {
+    float M = -INFINITY;
+    for (int j = lane; j < nparts; j += 32)
+      M = fmaxf(M, __ldcg(a.part_ml + (static_cast<int64_t>(vf + j + p) * G + hg) * 2));
+    M = warp_max_xor(M, 1, 16);
+    const float m_use = M == -INFINITY ? 0.f : M;
+    float L = 0.f;
+    for (int j = lane; j < nparts; j += 32) {
+      const float2 ml =
+          __ldcg(reinterpret_cast<const float2*>(a.part_ml + (static_cast<int64_t>(vf + j + p) * G + hg) * 2));
+      const float w = exp2f(ml.x - m_use);
+      s_w[j * G + hg] = w;
+      L += ml.y * w;
+    }
+    L = warp_sum_xor(L, 1, 16);
+    if (lane == 0) {
+      s_inv[hg] = 1.f / fmaxf(L, 1e-12f);
+      if (a.lse != nullptr)
+        a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg] =
+            (M == -INFINITY || L <= 0.f) ? -INFINITY : M * kLn2 + logf(L);
+    }
+  }
+  consumer_barrier(kConsumers);
+  // O: E = G*D/4 float4 elements, `groups` threads per element split the parts
+  const int E = G * (D / 4);
+  const int groups = E >= kConsumers ? 1 : kConsumers / E;
+  T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
+  for (int e0 = 0; e0 < E; e0 += kConsumers / groups) {
+    const int e = e0 + tid % (kConsumers / groups);
+    const int grp = tid / (kConsumers / groups);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool active = e < E && grp < groups;
+    const int hg = e / (D / 4), d4 = e - (e / (D / 4)) * (D / 4);
+    if (active) {
+#pragma unroll 4
+      for (int j = grp; j < nparts; j += groups) {
+        const float w = s_w[j * G + hg];
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(
+            a.part_o + (static_cast<int64_t>(vf + j + p) * G + hg) * D + d4 * 4));
+        acc.x += w * o.x;
+        acc.y += w * o.y;
+        acc.z += w * o.z;
+        acc.w += w * o.w;
+      }
+    }
+    if (groups > 1) {
+      if (active) s_red[grp * (kConsumers / groups) + (e - e0)] = acc;
+      consumer_barrier(kConsumers);
+      if (active && grp == 0) {
+        for (int q = 1; q < groups; ++q) {
+          const float4 r = s_red[q * (kConsumers / groups) + (e - e0)];
+          acc.x += r.x;
+          acc.y += r.y;
+          acc.z += r.z;
+          acc.w += r.w;
+        }
+      }
+    }
+    if (active && grp == 0) {
+      const float inv = s_inv[hg];
+      T* oh = out + static_cast<int64_t>(h * G + hg) * a.out_sh + d4 * 4;
+      oh[0] = from_float<T>(acc.x * inv);
+      oh[1] = from_float<T>(acc.y * inv);
+      oh[2] = from_float<T>(acc.z * inv);
+      oh[3] = from_float<T>(acc.w * inv);
+    }
+    if (groups > 1) consumer_barrier(kConsumers);
+  }
+}
+
+template <int D>
+struct Layout {
+  static constexpr int NCW = D <= 128 ? 8 : 4;  // consumer warps (= workers) per CTA
+  static constexpr int kThreads = (NCW + 1) * 32;
+  static constexpr int kTileBytes = kTileRows * D * 2;
+  static constexpr int kStageBytes = NCW * 2 * kTileBytes;
+  static constexpr int NS = kStageBudget / kStageBytes;
+  static_assert(NS >= 2, "tile ring needs at least two stages");
+  static constexpr size_t smem_bytes(int batch) {
+    return 1024 + NS * kStageBytes + 2 * NS * sizeof(uint64_t) + (batch + 1) * sizeof(int);
+  }
+};
+
+template <typename T, int D, int NT>
+__global__ void __launch_bounds__(Layout<D>::kThreads, 1)
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tmap, const DecodeArgs a) {
+  using L = Layout<D>;
+  constexpr int NCW = L::NCW;
+  constexpr int kTileBytes = L::kTileBytes;
+  constexpr int kStageBytes = L::kStageBytes;
+  constexpr int NS = L::NS;
+  constexpr int kBoxes = D / 64;
+  constexpr int kConsumers = NCW * 32;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int s_flag, s_abort;
+  uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * kStageBytes);
+  uint64_t* empty = full + NS;
+  int* s_cum = reinterpret_cast<int*>(empty + NS);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 0) build_prefix(a, s_cum, lane);
+  if (threadIdx.x == 32) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], NCW);
+    }
+    fence_barrier_init();
+    s_abort = 0;
+  }
+  __syncthreads();
+
+  // Pairs without tokens: zero output, LSE = -inf.
+  for (int p = blockIdx.x; p < a.batch * a.hkv; p += gridDim.x) {
+    const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
+    if (s_cum[b + 1] != s_cum[b]) continue;
+    T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
+    for (int e = threadIdx.x; e < a.group * D; e += blockDim.x)
+      out[static_cast<int64_t>(h * a.group + e / D) * a.out_sh + e % D] = from_float<T>(0.f);
+    if (a.lse != nullptr && threadIdx.x < a.group)
+      a.lse[static_cast<int64_t>(b) * a.hq + h * a.group + threadIdx.x] = -INFINITY;
+  }
+
+  const int total = s_cum[a.batch] * a.hkv;
+  if (total == 0) return;
+  const int W = div_up(total, a.num_workers);
+  const int v0 = blockIdx.x * NCW;
+  const int n_stages = max(0, min(W, total - v0 * W));
+  if (n_stages == 0) return;
+
+  if (warp == NCW) {
+    // ================================ producer ================================
+    prefetch_tensormap(&tmap);
+    const int w = lane % NCW, j = lane / NCW;  // this lane's worker / stage in window
+    constexpr int kWin = 32 / NCW;
+    const int worker_first = (v0 + w) * W;
+    const int worker_len = max(0, min(W, total - worker_first));
+    const int64_t kv_rows = static_cast<int64_t>(a.hkv) * a.page_size;
+
+    auto rows_of = [&](int s, int& row_k, bool& ok) {
+      ok = s < worker_len;
+      row_k = 0;
+      if (!ok) return;
+      const TilePos p = locate(s_cum, a.batch, a.hkv, worker_first + s);
+      const int page = p.t / a.tiles_per_page;
+      const int row_off = (p.t - page * a.tiles_per_page) * kTileRows;
+      int slot = a.page_table[static_cast<int64_t>(p.b) * a.pt_sb + page];
+      if (slot < 0 || slot >= a.pool_pages) {
+        report_status(HELM_DEV_BAD_PAGE);
+        slot = 0;
+      }
+      row_k = static_cast<int>((static_cast<int64_t>(slot) * 2 * a.hkv + p.h) * a.page_size +
+                               row_off);
+    };
+
+    int row_cur, row_nxt;
+    bool ok_cur, ok_nxt;
+    rows_of(j, row_cur, ok_cur);
+    for (int win = 0; win * kWin < n_stages; ++win) {
+      rows_of((win + 1) * kWin + j, row_nxt, ok_nxt);  // next window's page-table reads
+      for (int jj = 0; jj < kWin; ++jj) {
+        const int s = win * kWin + jj;
+        if (s >= n_stages) break;
+        const int buf = s % NS, n = s / NS;
+        int alive = 1;
+        if (lane == 0 && n > 0) alive = mbar_wait(&empty[buf], (n - 1) & 1) ? 1 : 0;
+        alive = __shfl_sync(0xffffffffu, alive, 0);
+        if (!alive) return;
+        const bool mine = (j == jj) && ok_cur;
+        const unsigned issuing = __ballot_sync(0xffffffffu, mine);
+        if (lane == 0) mbar_arrive_expect_tx(&full[buf], __popc(issuing) * 2 * kTileBytes);
+        __syncwarp();
+        if (mine) {
+          uint8_t* kdst = smem + buf * kStageBytes + w * 2 * kTileBytes;
+          uint8_t* vdst = kdst + kTileBytes;
+          const int row_v = static_cast<int>(row_cur + kv_rows);
+#pragma unroll
+          for (int hb = 0; hb < kBoxes; ++hb) {
+            tma_load_2d(kdst + hb * 2048, &tmap, hb * 64, row_cur, &full[buf]);
+            tma_load_2d(vdst + hb * 2048, &tmap, hb * 64, row_v, &full[buf]);
+          }
+        }
+      }
+      row_cur = row_nxt;
+      ok_cur = ok_nxt;
+    }
+    return;
+  }
+
+  // ================================= consumers ================================
+  const int v = v0 + warp;
+  const int first = v * W;
+  const int my_len = max(0, min(W, total - first));
+  Worker<T, D, NT> st;
+  TilePos pos;
+  if (my_len > 0) pos = locate(s_cum, a.batch, a.hkv, first);
+  const uint32_t ring = smem_addr(smem);
+  bool ok = true;
+
+  for (int s = 0; s < n_stages; ++s) {
+    const int buf = s % NS, n = s / NS;
+    if (!mbar_wait(&full[buf], n & 1)) {
+      ok = false;
+      break;
+    }
+    if (s < my_len) {
+      if (pos.b != st.cur_b || pos.h != st.cur_h) {
+        if (st.cur_b >= 0) st.flush(a, s_cum, W, v, lane);
+        st.cur_b = pos.b;
+        st.cur_h = pos.h;
+        st.reset();
+        st.load_q(a, pos.b, pos.h, lane);
+      }
+      const int page = pos.t / a.tiles_per_page;
+      const int row_off = (pos.t - page * a.tiles_per_page) * kTileRows;
+      int page_tokens, tok0;
+      if (a.num_pages != nullptr) {
+        const int64_t e = static_cast<int64_t>(pos.b) * a.pt_sb + page;
+        page_tokens = min(a.page_used[e], a.page_size);
+        tok0 = a.page_start[e] + row_off;
+      } else {
+        page_tokens = min(a.page_size, a.kv_lens[pos.b] - page * a.page_size);
+        tok0 = page * a.page_size + row_off;
+      }
+      const int valid = max(0, min(kTileRows, page_tokens - row_off));
+      const uint32_t kb = ring + buf * kStageBytes + warp * 2 * kTileBytes;
+      st.tile(a, kb, kb + kTileBytes, valid, tok0, pos.b, lane);
+      advance(pos, s_cum, a.batch, a.hkv);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[buf]);
+  }
+  if (!ok) {
+    if (lane == 0) s_abort = 1;
+  } else if (st.cur_b >= 0) {
+    st.flush(a, s_cum, W, v, lane);
+  }
+
+  // ============ merge: the last CTA to finish a split pair combines it ============
+  __threadfence();
+  consumer_barrier(kConsumers);
+  if (s_abort) return;  // every consumer warp reads the same flag after the barrier
+  const int x0 = v0 * W, x1 = min((v0 + NCW) * W, total);
+  const TilePos pf = locate(s_cum, a.batch, a.hkv, x0);
+  const TilePos pl = locate(s_cum, a.batch, a.hkv, x1 - 1);
+  for (int p = pf.b * a.hkv + pf.h; p <= pl.b * a.hkv + pl.h; ++p) {
+    const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
+    const int tb = s_cum[b + 1] - s_cum[b];
+    if (tb == 0) continue;
+    const int stt = s_cum[b] * a.hkv + h * tb;
+    const int vf = stt / W, vl = (stt + tb - 1) / W;
+    if (vf == vl) continue;  // one worker covered it and wrote the output
+    if (threadIdx.x == 0) {
+      const int old = atomicAdd(a.counters + p, 1);
+      s_flag = (old == vl / NCW - vf / NCW) ? 1 : 0;
+      __threadfence();
+    }
+    consumer_barrier(kConsumers);
+    if (s_flag) {
+      merge_pair<T, D, NCW>(a, p, vf, vl, smem);
+      consumer_barrier(kConsumers);
+      if (threadIdx.x == 0) a.counters[p] = 0;  // ready for the next call
+    }
+    consumer_barrier(kConsumers);
+  }
+}
+
+// ----------------------------------------------------------------- host side --
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+template <typename T, int D, int NT>
+int launch(const DecodeArgs& a, const void* pool, int64_t pool_rows, int grid,
+           cudaStream_t stream) {
+  using L = Layout<D>;
+  static unsigned long long configured = 0;  // one bit per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return HELM_ERR_CUDA;
+  if (dev >= 64) return HELM_ERR_UNSUPPORTED;
+  if (!(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(paged_decode_kernel<T, D, NT>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(L::smem_bytes(kMaxBatch))) != cudaSuccess)
+      return HELM_ERR_CUDA;
+    configured |= 1ull << dev;
+  }
+  EncodeTiledFn encode = get_encode_fn();
+  if (encode == nullptr) return HELM_ERR_CUDA;
+  CUtensorMap map;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(pool_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
+  cuuint32_t box[2] = {64, kTileRows};
+  cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType dt = std::is_same<T, __nv_bfloat16>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  if (encode(&map, dt, 2, const_cast<void*>(pool), dims, strides, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return HELM_ERR_CUDA;
+  DecodeArgs args = a;
+  args.num_workers = grid * L::NCW;
+  paged_decode_kernel<T, D, NT>
+      <<<grid, L::kThreads, L::smem_bytes(a.batch), stream>>>(map, args);
+  if (cudaGetLastError() != cudaSuccess) return HELM_ERR_CUDA;
+  return HELM_OK;
+}
+
+template <typename T, int D>
+int dispatch_nt(const DecodeArgs& a, const void* pool, int64_t rows, int grid, cudaStream_t s) {
+  if (a.group <= 8) return launch<T, D, 1>(a, pool, rows, grid, s);
+  return launch<T, D, 2>(a, pool, rows, grid, s);
+}
+
+template <typename T>
+int dispatch_d(int head_dim, const DecodeArgs& a, const void* pool, int64_t rows, int grid,
+               cudaStream_t s) {
+  switch (head_dim) {
+    case 64:
+      return dispatch_nt<T, 64>(a, pool, rows, grid, s);
+    case 128:
+      return dispatch_nt<T, 128>(a, pool, rows, grid, s);
+    case 256:
+      return dispatch_nt<T, 256>(a, pool, rows, grid, s);
+    default:
+      return HELM_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+int64_t paged_decode_slots(int batch, int num_kv_heads) {
+  return static_cast<int64_t>(num_sms_current_device()) * kMaxNCW +
+         static_cast<int64_t>(batch) * num_kv_heads;
+}
+
+// Workspace: per-pair counters [B*Hkv] int32 | partial O [slots][G][D] fp32 |
+// partial (m, l) [slots][G][2] fp32, each region 256-byte aligned.  The
+// counters (the first roundup(4*B*Hkv, 256) bytes) must be zero when a call
+// starts; a call that completes leaves them zero.
+struct WorkspaceLayout {
+  int64_t o_bytes, ml_bytes, cnt_bytes;
+  WorkspaceLayout(int batch, int hq, int hkv, int d) {
+    const int64_t group = hq / hkv;
+    const int64_t slots = paged_decode_slots(batch, hkv);
+    o_bytes = ((slots * group * d * 4 + 255) / 256) * 256;
+    ml_bytes = ((slots * group * 2 * 4 + 255) / 256) * 256;
+    cnt_bytes = ((static_cast<int64_t>(batch) * hkv * 4 + 255) / 256) * 256;
+  }
+  int64_t total() const { return o_bytes + ml_bytes + cnt_bytes; }
+};
+
+}  // namespace helm
+
+using helm::DecodeArgs;
+
+extern "C" int64_t helm_paged_decode_workspace_bytes(int batch, int num_q_heads,
+                                                     int num_kv_heads, int head_dim) {
+  if (batch <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || head_dim <= 0) return 0;
+  return helm::WorkspaceLayout(batch, num_q_heads, num_kv_heads, head_dim).total();
+}
+
+extern "C" int helm_paged_decode_attention(
+    const void* q, int64_t q_stride_b, int64_t q_stride_h, const void* kv_pool, int64_t pool_pages,
+    const int32_t* page_table, int64_t pt_stride_b, int max_pages, const int32_t* kv_lens,
+    const int32_t* num_pages, const int32_t* page_used, const int32_t* page_start,
+    const void* mask, int mask_dtype, int64_t mask_stride_b, void* out, int64_t out_stride_b,
+    int64_t out_stride_h, float* lse, void* workspace, int64_t workspace_bytes, int batch,
+    int num_q_heads, int num_kv_heads, int head_dim, int page_size, int dtype, float scale,
+    float softcap, int max_kv_len_hint, void* stream) {
+  using namespace helm;
+  if (q == nullptr || kv_pool == nullptr || page_table == nullptr || kv_lens == nullptr ||
+      out == nullptr || workspace == nullptr)
+    return HELM_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || page_size <= 0 || max_pages < 0 ||
+      pool_pages <= 0)
+    return HELM_ERR_INVALID_ARGUMENT;
+  if (num_q_heads % num_kv_heads != 0) return HELM_ERR_INVALID_ARGUMENT;
+  const int group = num_q_heads / num_kv_heads;
+  if (group > 16) return HELM_ERR_UNSUPPORTED;
+  if (batch > kMaxBatch) return HELM_ERR_UNSUPPORTED;
+  if (dtype != HELM_DTYPE_BF16 && dtype != HELM_DTYPE_FP16) return HELM_ERR_UNSUPPORTED;
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return HELM_ERR_UNSUPPORTED;
+  const bool ragged = num_pages != nullptr;
+  if (ragged != (page_used != nullptr) || ragged != (page_start != nullptr))
+    return HELM_ERR_INVALID_ARGUMENT;
+  if (mask != nullptr && mask_dtype != HELM_DTYPE_FP32 && mask_dtype != HELM_DTYPE_BF16 &&
+      mask_dtype != HELM_DTYPE_FP16)
+    return HELM_ERR_INVALID_ARGUMENT;
+  // q rows are read as 32-bit words, the pool through TMA (16-byte rule).
+  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_stride_b & 1) || (q_stride_h & 1))
+    return HELM_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(kv_pool) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return HELM_ERR_ALIGNMENT;
+  const int64_t pool_rows = pool_pages * 2 * num_kv_heads * static_cast<int64_t>(page_size);
+  if (pool_rows >= (int64_t(1) << 31)) return HELM_ERR_UNSUPPORTED;
+  if (workspace_bytes <
+      helm_paged_decode_workspace_bytes(batch, num_q_heads, num_kv_heads, head_dim))
+    return HELM_ERR_WORKSPACE;
+
+  const WorkspaceLayout ws(batch, num_q_heads, num_kv_heads, head_dim);
+  DecodeArgs a;
+  a.q = q;
+  a.q_sb = q_stride_b;
+  a.q_sh = q_stride_h;
+  a.pool_pages = pool_pages;
+  a.page_table = page_table;
+  a.pt_sb = pt_stride_b;
+  a.max_pages = max_pages;
+  a.kv_lens = kv_lens;
+  a.num_pages = num_pages;
+  a.page_used = page_used;
+  a.page_start = page_start;
+  a.mask = mask;
+  a.mask_dtype = mask_dtype;
+  a.mask_sb = mask_stride_b;
+  a.out = out;
+  a.out_sb = out_stride_b;
+  a.out_sh = out_stride_h;
+  a.lse = lse;
+  a.counters = static_cast<int*>(workspace);
+  a.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ws.cnt_bytes);
+  a.part_ml =
+      reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ws.cnt_bytes + ws.o_bytes);
+  a.batch = batch;
+  a.hq = num_q_heads;
+  a.hkv = num_kv_heads;
+  a.group = group;
+  a.page_size = page_size;
+  a.tiles_per_page = (page_size + kTileRows - 1) / kTileRows;
+  a.scale = scale;
+  a.scale_log2 = scale * kLog2e;
+  a.softcap = softcap;
+
+  const int sms = num_sms_current_device();
+  int grid = sms;
+  if (max_kv_len_hint > 0) {
+    const int64_t pages = (static_cast<int64_t>(max_kv_len_hint) + page_size - 1) / page_size;
+    const int64_t tiles = pages * a.tiles_per_page * batch * num_kv_heads;
+    const int ncw = head_dim <= 128 ? 8 : 4;
+    const int64_t want = (tiles + ncw * kMinTilesPerWorker - 1) / (ncw * kMinTilesPerWorker);
+    grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, want)));
+  }
+  a.num_workers = 0;  // set by launch() from the CTA shape of the head_dim
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int rc = dtype == HELM_DTYPE_BF16
+               ? dispatch_d<__nv_bfloat16>(head_dim, a, kv_pool, pool_rows, grid, s)
+               : dispatch_d<__half>(head_dim, a, kv_pool, pool_rows, grid, s);
+  if (rc == HELM_ERR_CUDA) set_last_cuda_error(cudaGetLastError());
+  return rc;
+}

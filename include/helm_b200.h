@@ -1,0 +1,194 @@
+/*
+ * helm_b200 — C ABI of the B200-native paged-KV decode path.
+ *
+ * This library replaces the eager-PyTorch KV-cache / attention path of HELM
+ * (helm/runtime/kv_cache.py, kv_allocator.py, kv_offload.py).  Every entry
+ * point takes plain device pointers, element strides and sizes, runs on the
+ * CUDA stream it is given (a cudaStream_t passed as void*), never allocates
+ * or frees caller memory, and returns an int status (HELM_OK on success).
+ *
+ * KV page pool layout (one contiguous allocation per device or host tier):
+ *     pool[slot][kv][head][token][dim]      kv = 0 for K, 1 for V
+ * i.e. a page slot holds K then V for all KV heads, each head's page_size x
+ * head_dim block contiguous.  One (page, head) block is therefore a dense
+ * page_size*head_dim*elt byte run (4 KiB for 16 bf16 tokens at head_dim 128).
+ *
+ * Data types: HELM_DTYPE_BF16 / HELM_DTYPE_FP16 for K, V, Q and outputs;
+ * masks may also be HELM_DTYPE_FP32.  Softmax state is always fp32.
+ */
+#ifndef HELM_B200_H_
+#define HELM_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (host return values) ---------------------------------- */
+#define HELM_OK 0
+#define HELM_ERR_INVALID_ARGUMENT 1
+#define HELM_ERR_UNSUPPORTED 2
+#define HELM_ERR_CUDA 3
+#define HELM_ERR_WORKSPACE 4
+#define HELM_ERR_ALIGNMENT 5
+
+/* ---- device status bits (read with helm_get_device_status) --------------- */
+#define HELM_DEV_TIMEOUT 1u   /* a bounded wait inside a kernel gave up      */
+#define HELM_DEV_BAD_PAGE 2u  /* a page-table entry or page count was out of */
+                              /* range; the access was skipped / clamped     */
+
+/* ---- data types ------------------------------------------------------------ */
+#define HELM_DTYPE_FP32 0
+#define HELM_DTYPE_FP16 1
+#define HELM_DTYPE_BF16 2
+
+/* Library version (major*10000 + minor*100 + patch). */
+int helm_version(void);
+
+/* Human-readable text for a status code. */
+const char* helm_status_string(int status);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+const char* helm_last_cuda_error(void);
+
+/*
+ * Reads the device status word of the current device into *out (after
+ * synchronising `stream`), and clears it when `reset` is non-zero.
+ * No reference counterpart: the reference raises Python exceptions
+ * synchronously (kv_allocator.py:128-140, kv_cache.py:208); kernels here
+ * record errors instead of trapping.
+ */
+int helm_get_device_status(unsigned int* out, int reset, void* stream);
+
+/*
+ * Bytes of fp32 scratch that helm_paged_decode_attention needs for the given
+ * shape on the current device (split-KV partial softmax states).
+ */
+int64_t helm_paged_decode_workspace_bytes(int batch, int num_q_heads, int num_kv_heads,
+                                          int head_dim);
+
+/*
+ * Paged decode attention for one query position per sequence:
+ *     O[b,h,:] = softmax(scale * q[b,h,:] . K[b,kvh(h),t,:]^T  (+softcap) (+mask[b,t])) V
+ * over the tokens t of sequence b, GQA mapping kvh(h) = h / (Hq/Hkv), fp32
+ * accumulation, O in the query dtype, LSE = logsumexp of the same scores (fp32,
+ * natural log; -inf for an empty sequence, whose O is zero).
+ *
+ * Replaces perform_streaming_attention (helm/runtime/kv_cache.py:405-662) and
+ * the paged branches of _decode_batched (helm/runtime/kv_offload.py:144-186).
+ *
+ *  q            [B, Hq, D] with element strides q_stride_b, q_stride_h (dim stride 1)
+ *  kv_pool      page pool (layout above), pool_pages slots
+ *  page_table   int32 [B, max_pages] (row stride pt_stride_b): pool slot of page i
+ *  kv_lens      int32 [B]: tokens of sequence b
+ *  num_pages,   optional (all NULL or all set): ragged page lists.  When NULL,
+ *  page_used,   page i of sequence b holds min(page_size, kv_len - i*page_size)
+ *  page_start   tokens.  When set, sequence b has num_pages[b] pages, page i
+ *               holds page_used[b*pt_stride_b+i] tokens whose first logical
+ *               position is page_start[b*pt_stride_b+i].
+ *  mask         optional additive key mask [B, T] (row stride mask_stride_b),
+ *               indexed by logical token position, dtype mask_dtype
+ *  softcap      tanh soft-capping of the scaled scores when > 0
+ *  out          [B, Hq, D] strides out_stride_b, out_stride_h
+ *  lse          optional fp32 [B, Hq]
+ *  workspace    >= helm_paged_decode_workspace_bytes(...) bytes, 256-byte aligned.
+ *               Its first roundup(4*batch*num_kv_heads, 256) bytes are per-pair
+ *               counters that must be zero when the call starts (zero-fill a
+ *               new workspace); a call that completes leaves them zero, but the
+ *               bytes after them are overwritten, so re-zero that prefix when
+ *               a call uses a larger batch*num_kv_heads than the previous one.
+ *  max_kv_len_hint  upper bound on kv_lens (0 = unknown); sizes the grid
+ */
+int helm_paged_decode_attention(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                const void* kv_pool, int64_t pool_pages,
+                                const int32_t* page_table, int64_t pt_stride_b, int max_pages,
+                                const int32_t* kv_lens, const int32_t* num_pages,
+                                const int32_t* page_used, const int32_t* page_start,
+                                const void* mask, int mask_dtype, int64_t mask_stride_b,
+                                void* out, int64_t out_stride_b, int64_t out_stride_h, float* lse,
+                                void* workspace, int64_t workspace_bytes, int batch,
+                                int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                int dtype, float scale, float softcap, int max_kv_len_hint,
+                                void* stream);
+
+/*
+ * Fused KV append: optional per-head RMSNorm of q and k (fp32 variance,
+ * eps, weight * normed.to(dtype)), optional rotary embedding with the
+ * caller's cos/sin tables (HF rotate_half convention), then the K and V rows
+ * of every token are written into the page pool at row slot_rows[token] =
+ * slot*page_size + row_in_page (a negative entry skips the token).  The
+ * processed q is written to q_out.
+ *
+ * Replaces the q_norm/k_norm + apply_rotary_pos_emb of the patched attention
+ * forwards (helm/runtime/kv_offload.py:368-373) and the page writes of
+ * KVCacheManager.append_decode / append_prefill (helm/runtime/kv_cache.py:
+ * 113-171).
+ *
+ *  q, k, v      [N tokens, H, D] with token strides q_stride_t, k_stride_t,
+ *               v_stride_t and head strides q_stride_h, k_stride_h, v_stride_h
+ *  q_norm_w,    [D] RMSNorm weights (NULL: no norm)
+ *  k_norm_w
+ *  cos, sin     [N, D] rotary tables in the model dtype (NULL: no rotation),
+ *               token stride rope_stride_t
+ *  q_out        [N, Hq, D], strides q_out_stride_t, q_out_stride_h (may be NULL)
+ *  k_out, v_out optional copies of the processed K/V rows ([N, Hkv, D] dense)
+ */
+int helm_kv_append(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
+                   int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
+                   int64_t v_stride_h, const void* q_norm_w, const void* k_norm_w, float eps,
+                   const void* cos, const void* sin, int64_t rope_stride_t, void* q_out,
+                   int64_t q_out_stride_t, int64_t q_out_stride_h, void* k_out, void* v_out,
+                   void* kv_pool, int64_t pool_pages, const int64_t* slot_rows, int num_tokens,
+                   int num_q_heads, int num_kv_heads, int head_dim, int page_size, int dtype,
+                   void* stream);
+
+/*
+ * Copies whole page slots between two pools (device <-> pinned host, or
+ * device <-> device): dst_pool[dst_slots[i]] = src_pool[src_slots[i]] for
+ * i < n.  Slot lists are HOST int64 arrays; runs of consecutive slots are
+ * merged into one cudaMemcpyAsync each.  Both pools must be reachable from
+ * the copy engine (device memory or page-locked host memory).
+ *
+ * Replaces KVAllocator.move_page (helm/runtime/kv_allocator.py:95-144) and the
+ * per-page CPU->GPU stream copies of perform_streaming_attention
+ * (helm/runtime/kv_cache.py:482-530, :624-659).
+ */
+int helm_copy_pages(void* dst_pool, const void* src_pool, int64_t page_bytes,
+                    const int64_t* dst_slots, const int64_t* src_slots, int64_t n, void* stream);
+
+/*
+ * Gathers paged K/V into dense tensors K_out, V_out [B, Hkv, T_max, D]
+ * (token positions >= kv_lens[b] are zero-filled).  Used where a dense
+ * library attention is called on paged data (chunked prefill).
+ *
+ * Replaces the torch.cat page concatenation of perform_streaming_attention
+ * (helm/runtime/kv_cache.py:563-564) and _decode_batched
+ * (helm/runtime/kv_offload.py:160-171).
+ */
+int helm_gather_kv(const void* kv_pool, int64_t pool_pages, const int32_t* page_table,
+                   int64_t pt_stride_b, int max_pages, const int32_t* kv_lens, void* k_out,
+                   void* v_out, int batch, int num_kv_heads, int head_dim, int page_size,
+                   int t_max, int dtype, void* stream);
+
+/*
+ * Merges R partial attention states over disjoint key ranges:
+ *     M = max_r lse[r];  w_r = exp(lse[r] - M)
+ *     out = sum_r w_r * o[r] / sum_r w_r,   lse_out = M + log(sum_r w_r)
+ * o_parts [R, rows, D] (dtype o_dtype: fp32, bf16 or fp16), lse_parts fp32
+ * [R, rows]; out [rows, D] in out_dtype; lse_out optional fp32 [rows].
+ * rows = batch * num_q_heads.  A part with lse = -inf contributes nothing.
+ *
+ * No single-device counterpart in the reference (it is single-GPU); this is
+ * the cross-rank form of its running-max rescale (helm/runtime/kv_cache.py:
+ * 523-529) used by the sequence-split path.
+ */
+int helm_merge_attention_states(const void* o_parts, int o_dtype, const float* lse_parts,
+                                int num_parts, int64_t rows, int head_dim, void* out,
+                                int out_dtype, float* lse_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HELM_B200_H_ */
