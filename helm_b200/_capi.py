@@ -41,6 +41,10 @@ _SIGNATURES = {
         _P, _I64,                  # workspace, bytes
         _I, _I, _I, _I, _I, _I,    # batch, hq, hkv, head_dim, page_size, dtype
         _F, _F, _I, _P]),          # scale, softcap, max_kv_len_hint, stream
+    "helm_paged_decode_attention_noalloc": (_I, [
+        _P, _I64, _I64, _P, _I64, _P, _I64, _I, _P, _P, _P, _P,
+        _P, _I, _I64, _P, _I64, _I64, _P,
+        _I, _I, _I, _I, _I, _I, _F, _F, _I, _P]),
     "helm_kv_append": (_I, [
         _P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I64,   # q, k, v
         _P, _P, _F,                                       # norm weights, eps

@@ -8,6 +8,7 @@
 #include "kv_append.cu"
 #include "kv_ops.cu"
 #include "paged_attention.cu"
+#include "paged_attention_noalloc.cu"
 
 namespace helm {
 

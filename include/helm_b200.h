@@ -113,6 +113,34 @@ int helm_paged_decode_attention(const void* q, int64_t q_stride_b, int64_t q_str
                                 void* stream);
 
 /*
+ * Same computation and arguments as helm_paged_decode_attention, without the
+ * workspace: for callers that cannot allocate device memory, such as a server
+ * that gives all of HBM to its own pool at start-up (a later cudaMalloc would
+ * fail or fragment it) or a decode loop that must not stall on the device-wide
+ * synchronisation of cudaFree.  It has no counterpart in the reference (HELM
+ * allocates freely through PyTorch).
+ *
+ * Scratch comes from a fixed 8 MiB array inside the library, held by every GPU
+ * that loads it until exit; shapes needing more (see
+ * helm_paged_decode_workspace_bytes) return HELM_ERR_WORKSPACE.  The first call
+ * on a device sets up that device's scratch address: make it before any stream
+ * capture.  All calls share the array, so calls that overlap on the GPU race;
+ * keep them ordered on one stream.  Each call clears the counters it needs on
+ * `stream` first and allocates nothing.
+ */
+int helm_paged_decode_attention_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                        const void* kv_pool, int64_t pool_pages,
+                                        const int32_t* page_table, int64_t pt_stride_b,
+                                        int max_pages, const int32_t* kv_lens,
+                                        const int32_t* num_pages, const int32_t* page_used,
+                                        const int32_t* page_start, const void* mask,
+                                        int mask_dtype, int64_t mask_stride_b, void* out,
+                                        int64_t out_stride_b, int64_t out_stride_h, float* lse,
+                                        int batch, int num_q_heads, int num_kv_heads,
+                                        int head_dim, int page_size, int dtype, float scale,
+                                        float softcap, int max_kv_len_hint, void* stream);
+
+/*
  * Fused KV append: optional per-head RMSNorm of q and k (fp32 variance,
  * eps, weight * normed.to(dtype)), optional rotary embedding with the
  * caller's cos/sin tables (HF rotate_half convention), then the K and V rows
