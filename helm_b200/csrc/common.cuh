@@ -39,6 +39,19 @@ __device__ __forceinline__ void report_status(unsigned int bits) {
 // abandons its work.
 constexpr long long kWaitBudgetCycles = 2000000000LL;
 
+// atomicAdd with acquire+release semantics at GPU scope.  After a CTA barrier,
+// one thread's call publishes every write the CTA made before the barrier and,
+// when it observes another CTA's count, makes that CTA's writes visible to the
+// CTA once the following barrier has passed.
+__device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -58,8 +58,10 @@ struct DecodeArgs {
   void* out;
   int64_t out_sb, out_sh;
   float* lse;
-  float* part_o;    // [slots][G][D]
-  float* part_ml;   // [slots][G][2]  (m in log2 units, l)
+  float* part_o;    // warp partials [num_workers + pairs][G][D]
+  float* part_ml;   // warp partials [num_workers + pairs][G][2]  (m in log2 units, l)
+  float* cta_o;     // CTA partials [grid + pairs][G][D]
+  float* cta_ml;    // CTA partials [grid + pairs][G][2]
   int* counters;    // [B * Hkv] CTAs done per pair; zero between calls
   int batch, hq, hkv, group, page_size, tiles_per_page;
   float scale;
@@ -162,6 +164,7 @@ struct Worker {
   float o[NT][KS][4];
   uint32_t qf[NT][KS][2];
   int cur_b = -1, cur_h = -1;
+  int cur_len = 0;  // kv_len of the current sequence (dense page lists)
 
   __device__ __forceinline__ void reset() {
 #pragma unroll
@@ -236,6 +239,31 @@ struct Worker {
           }
           if (g == 0)
             *reinterpret_cast<float2*>(a.part_ml + slot * 2) = make_float2(m[nt][j], lt);
+        }
+      }
+    }
+  }
+
+  // Raw state (m, lane-reduced l, unnormalised O) into a shared-memory record
+  // laid out as m[16] | l[16] | O[16][D].
+  __device__ __forceinline__ void save(float* rec, int group, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float lt = warp_sum_xor(l[nt][j], 4, 16);
+        const int hg = nt * 8 + 2 * t + j;
+        if (hg >= group) continue;
+        float* o_rec = rec + 32 + hg * D;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+          o_rec[mt * 16 + g] = o[nt][mt][j];
+          o_rec[mt * 16 + 8 + g] = o[nt][mt][2 + j];
+        }
+        if (g == 0) {
+          rec[hg] = m[nt][j];
+          rec[16 + hg] = lt;
         }
       }
     }
@@ -339,86 +367,212 @@ __device__ __forceinline__ void consumer_barrier(int threads) {
   asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
 }
 
-// Merges the partial states of pair p (workers vf..vl) with the CTA's
-// consumer threads; `scratch` is the (now idle) tile ring.
+// Pair geometry in the flattened tile order: the workers (warps) that cover it
+// and whether the last of them goes on past it (then that worker flushed its
+// state for the pair to the warp-partial slot in mid-range).
+struct PairSpan {
+  int tiles, vf, vl;
+  bool last_continues;
+};
+
+__device__ __forceinline__ PairSpan pair_span(const DecodeArgs& a, const int* s_cum, int W,
+                                              int total, int p) {
+  const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
+  PairSpan ps;
+  ps.tiles = s_cum[b + 1] - s_cum[b];
+  ps.vf = ps.vl = 0;
+  ps.last_continues = false;
+  if (ps.tiles > 0) {
+    const int st = s_cum[b] * a.hkv + h * ps.tiles, en = st + ps.tiles;
+    ps.vf = st / W;
+    ps.vl = (en - 1) / W;
+    ps.last_continues = min((ps.vl + 1) * W, total) > en;
+  }
+  return ps;
+}
+
+// Combines K partial states of pair p into one: n_smem records in shared
+// memory (warps w0.. of this CTA), n_cta CTA partials at global slots
+// c0+k+p, and, when warp_slot >= 0, the warp partial at global slot
+// warp_slot+p.  Writes either the normalised output and LSE (final) or a CTA
+// partial at slot cta_out+p.  All consumer threads take part; global sources
+// are read with at most two dependent L2 round trips (all (m, l) at once,
+// then up to kBatch O values per element at once).
 template <typename T, int D, int NCW>
-__device__ void merge_pair(const DecodeArgs& a, int p, int vf, int vl, uint8_t* scratch) {
+__device__ void merge_sources(const DecodeArgs& a, int p, const float* s_states, int w0,
+                              int n_smem, int c0, int n_cta, int warp_slot, bool final_out,
+                              int cta_out, float* s_scratch) {
   constexpr int kConsumers = NCW * 32;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int G = a.group, nparts = vl - vf + 1;
-  const int b = p / a.hkv, h = p - b * a.hkv;
-  float* s_w = reinterpret_cast<float*>(scratch);       // [nparts][G] weights
-  float* s_inv = s_w + nparts * G;                        // [G]
-  float4* s_red =                                         // [kConsumers] group partial sums
-      reinterpret_cast<float4*>((reinterpret_cast<uintptr_t>(s_inv + 16) + 15) & ~uintptr_t(15));
-  // per head: M = max m_j, weights 2^(m_j - M), 1/L and LSE
-  for (int hg = warp; hg < G; hg += NCW) {
+  constexpr int kRec = 32 + 16 * D;
+  constexpr int kBatch = 8;
+  const int tid = threadIdx.x;
+  const int G = a.group;
+  const int K = n_smem + n_cta + (warp_slot >= 0 ? 1 : 0);
+  const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
+  float* s_m = s_scratch;        // [K][G]  m of each source, then its weight
+  float* s_l = s_m + K * G;      // [K][G]
+  float* s_M = s_l + K * G;      // [G]
+  float* s_L = s_M + 16;         // [G]
+
+  // global float offset of source k's record (O at og + hg*D, (m,l) at mlg + 2*hg)
+  auto src_o = [&](int k) -> const float* {
+    return k < n_smem + n_cta
+               ? a.cta_o + static_cast<int64_t>(c0 + k - n_smem + p) * G * D
+               : a.part_o + static_cast<int64_t>(warp_slot + p) * G * D;
+  };
+  auto src_ml = [&](int k) -> const float* {
+    return k < n_smem + n_cta
+               ? a.cta_ml + static_cast<int64_t>(c0 + k - n_smem + p) * G * 2
+               : a.part_ml + static_cast<int64_t>(warp_slot + p) * G * 2;
+  };
+  for (int e = tid; e < K * G; e += kConsumers) {
+    const int k = e / G, hg = e - (e / G) * G;
+    float m, l;
+    if (k < n_smem) {
+      m = s_states[(w0 + k) * kRec + hg];
+      l = s_states[(w0 + k) * kRec + 16 + hg];
+    } else {
+      const float2 v = __ldcg(reinterpret_cast<const float2*>(src_ml(k) + 2 * hg));
+      m = v.x;
+      l = v.y;
+    }
+    s_m[e] = m;
+    s_l[e] = l;
+  }
+  consumer_barrier(kConsumers);
+  if (tid < G) {
     float M = -INFINITY;
-    for (int j = lane; j < nparts; j += 32)
-      M = fmaxf(M, __ldcg(a.part_ml + (static_cast<int64_t>(vf + j + p) * G + hg) * 2));
-    M = warp_max_xor(M, 1, 16);
+    for (int k = 0; k < K; ++k) M = fmaxf(M, s_m[k * G + tid]);
     const float m_use = M == -INFINITY ? 0.f : M;
     float L = 0.f;
-    for (int j = lane; j < nparts; j += 32) {
-      const float2 ml =
-          __ldcg(reinterpret_cast<const float2*>(a.part_ml + (static_cast<int64_t>(vf + j + p) * G + hg) * 2));
-      const float w = exp2f(ml.x - m_use);
-      s_w[j * G + hg] = w;
-      L += ml.y * w;
+    for (int k = 0; k < K; ++k) {
+      const float w = exp2f(s_m[k * G + tid] - m_use);
+      s_m[k * G + tid] = w;  // weight replaces m
+      L += s_l[k * G + tid] * w;
     }
-    L = warp_sum_xor(L, 1, 16);
-    if (lane == 0) {
-      s_inv[hg] = 1.f / fmaxf(L, 1e-12f);
+    s_M[tid] = M;
+    s_L[tid] = L;
+  }
+  consumer_barrier(kConsumers);
+  T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
+  for (int e = tid; e < G * D; e += kConsumers) {
+    const int hg = e / D, d = e - (e / D) * D;
+    float acc = 0.f;
+    for (int k0 = 0; k0 < K; k0 += kBatch) {
+      float o[kBatch];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {  // issue every load of the batch first
+        const int k = k0 + i;
+        o[i] = 0.f;
+        if (k < K) {
+          if (k < n_smem)
+            o[i] = s_states[(w0 + k) * kRec + 32 + hg * D + d];
+          else
+            o[i] = __ldcg(src_o(k) + hg * D + d);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i)
+        if (k0 + i < K) acc += s_m[(k0 + i) * G + hg] * o[i];
+    }
+    if (final_out) {
+      out[static_cast<int64_t>(h * G + hg) * a.out_sh + d] =
+          from_float<T>(acc / fmaxf(s_L[hg], 1e-12f));
+    } else {
+      a.cta_o[(static_cast<int64_t>(cta_out + p) * G + hg) * D + d] = acc;
+    }
+  }
+  if (tid < G) {
+    const float M = s_M[tid], L = s_L[tid];
+    if (final_out) {
       if (a.lse != nullptr)
-        a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg] =
+        a.lse[static_cast<int64_t>(b) * a.hq + h * G + tid] =
             (M == -INFINITY || L <= 0.f) ? -INFINITY : M * kLn2 + logf(L);
+    } else {
+      *reinterpret_cast<float2*>(a.cta_ml + (static_cast<int64_t>(cta_out + p) * G + tid) * 2) =
+          make_float2(M, L);
     }
   }
   consumer_barrier(kConsumers);
-  // O: E = G*D/4 float4 elements, `groups` threads per element split the parts
-  const int E = G * (D / 4);
-  const int groups = E >= kConsumers ? 1 : kConsumers / E;
-  T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
-  for (int e0 = 0; e0 < E; e0 += kConsumers / groups) {
-    const int e = e0 + tid % (kConsumers / groups);
-    const int grp = tid / (kConsumers / groups);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const bool active = e < E && grp < groups;
-    const int hg = e / (D / 4), d4 = e - (e / (D / 4)) * (D / 4);
-    if (active) {
-#pragma unroll 4
-      for (int j = grp; j < nparts; j += groups) {
-        const float w = s_w[j * G + hg];
-        const float4 o = __ldcg(reinterpret_cast<const float4*>(
-            a.part_o + (static_cast<int64_t>(vf + j + p) * G + hg) * D + d4 * 4));
-        acc.x += w * o.x;
-        acc.y += w * o.y;
-        acc.z += w * o.z;
-        acc.w += w * o.w;
+}
+
+// One cross-CTA merge job: pair p, CTA partials at slots c0..c0+n_cta-1 (+p),
+// and the warp partial at slot warp_slot+p when warp_slot >= 0.
+struct MergeJob {
+  int p, c0, n_cta, warp_slot;
+};
+
+constexpr int kMaxDirectSources = 8;
+
+// Finishes several split pairs at once.  Each thread owns output elements
+// (job, head, dim) and loads the (m, l) and O value of every source of its
+// element together, so a job costs one dependent L2 round trip.  Jobs with
+// more than kMaxDirectSources sources are left to merge_sources.
+template <typename T, int D, int NCW>
+__device__ void merge_global(const DecodeArgs& a, const MergeJob* jobs, int n_jobs) {
+  constexpr int kConsumers = NCW * 32;
+  constexpr int kElems = 4;  // output elements per thread whose loads are in flight together
+  const int G = a.group;
+  const int per_job = G * D;
+  const int n_elem = n_jobs * per_job;
+  for (int e0 = 0; e0 < n_elem; e0 += kConsumers * kElems) {
+    float2 ml[kElems][kMaxDirectSources];
+    float o[kElems][kMaxDirectSources];
+    int K[kElems], hg[kElems], d[kElems], j[kElems];
+#pragma unroll
+    for (int i = 0; i < kElems; ++i) {
+      const int e = e0 + i * kConsumers + threadIdx.x;
+      K[i] = 0;
+      j[i] = 0;
+      hg[i] = 0;
+      d[i] = 0;
+      if (e < n_elem) {
+        j[i] = e / per_job;
+        const int r = e - j[i] * per_job;
+        hg[i] = r / D;
+        d[i] = r - hg[i] * D;
+        const MergeJob job = jobs[j[i]];
+        K[i] = job.n_cta + (job.warp_slot >= 0 ? 1 : 0);
+        if (K[i] > kMaxDirectSources) K[i] = 0;  // left to merge_sources
       }
-    }
-    if (groups > 1) {
-      if (active) s_red[grp * (kConsumers / groups) + (e - e0)] = acc;
-      consumer_barrier(kConsumers);
-      if (active && grp == 0) {
-        for (int q = 1; q < groups; ++q) {
-          const float4 r = s_red[q * (kConsumers / groups) + (e - e0)];
-          acc.x += r.x;
-          acc.y += r.y;
-          acc.z += r.z;
-          acc.w += r.w;
+#pragma unroll
+      for (int k = 0; k < kMaxDirectSources; ++k) {
+        ml[i][k] = make_float2(-INFINITY, 0.f);
+        o[i][k] = 0.f;
+        if (k < K[i]) {
+          const MergeJob job = jobs[j[i]];
+          const int64_t slot = k < job.n_cta ? static_cast<int64_t>(job.c0 + k + job.p)
+                                             : static_cast<int64_t>(job.warp_slot + job.p);
+          const float* mlp = (k < job.n_cta ? a.cta_ml : a.part_ml) + (slot * G + hg[i]) * 2;
+          const float* op = (k < job.n_cta ? a.cta_o : a.part_o) + (slot * G + hg[i]) * D + d[i];
+          ml[i][k] = __ldcg(reinterpret_cast<const float2*>(mlp));
+          o[i][k] = __ldcg(op);
         }
       }
     }
-    if (active && grp == 0) {
-      const float inv = s_inv[hg];
-      T* oh = out + static_cast<int64_t>(h * G + hg) * a.out_sh + d4 * 4;
-      oh[0] = from_float<T>(acc.x * inv);
-      oh[1] = from_float<T>(acc.y * inv);
-      oh[2] = from_float<T>(acc.z * inv);
-      oh[3] = from_float<T>(acc.w * inv);
+#pragma unroll
+    for (int i = 0; i < kElems; ++i) {
+      if (K[i] == 0) continue;
+      float M = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kMaxDirectSources; ++k) M = fmaxf(M, ml[i][k].x);
+      const float m_use = M == -INFINITY ? 0.f : M;
+      float L = 0.f, acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < kMaxDirectSources; ++k) {
+        const float w = k < K[i] ? exp2f(ml[i][k].x - m_use) : 0.f;
+        L += ml[i][k].y * w;
+        acc += o[i][k] * w;
+      }
+      const int p = jobs[j[i]].p;
+      const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
+      T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
+      out[static_cast<int64_t>(h * G + hg[i]) * a.out_sh + d[i]] =
+          from_float<T>(acc / fmaxf(L, 1e-12f));
+      if (d[i] == 0 && a.lse != nullptr)
+        a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg[i]] =
+            (M == -INFINITY || L <= 0.f) ? -INFINITY : M * kLn2 + logf(L);
     }
-    if (groups > 1) consumer_barrier(kConsumers);
   }
 }
 
@@ -447,7 +601,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   constexpr int kConsumers = NCW * 32;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ int s_flag, s_abort;
+  __shared__ int s_abort;
   uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * kStageBytes);
   uint64_t* empty = full + NS;
@@ -563,6 +717,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         if (st.cur_b >= 0) st.flush(a, s_cum, W, v, lane);
         st.cur_b = pos.b;
         st.cur_h = pos.h;
+        st.cur_len = a.num_pages != nullptr ? 0 : a.kv_lens[pos.b];
         st.reset();
         st.load_q(a, pos.b, pos.h, lane);
       }
@@ -574,7 +729,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         page_tokens = min(a.page_used[e], a.page_size);
         tok0 = a.page_start[e] + row_off;
       } else {
-        page_tokens = min(a.page_size, a.kv_lens[pos.b] - page * a.page_size);
+        page_tokens = min(a.page_size, st.cur_len - page * a.page_size);
         tok0 = page * a.page_size + row_off;
       }
       const int valid = max(0, min(kTileRows, page_tokens - row_off));
@@ -585,36 +740,92 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[buf]);
   }
+  // ============ merge ============
+  // 1. each warp's end-of-range state (if it does not cover its pair alone)
+  //    goes to a shared-memory record (the tile ring is idle now);
+  // 2. warps of this CTA ending in the same pair are combined: the final
+  //    output when this CTA covers the whole pair, else one CTA partial;
+  // 3. for pairs split across CTAs, every CTA touching the pair bumps its
+  //    counter after writing; the CTA that completes the count merges the
+  //    CTA partials (plus the mid-range warp partial, if any) and resets it.
+  constexpr int kRec = 32 + 16 * D;
+  float* s_states = reinterpret_cast<float*>(smem);
+  float* s_scratch = s_states + NCW * kRec;
+  __shared__ int s_endpair[NCW];
+  int end_pair = -1;
   if (!ok) {
     if (lane == 0) s_abort = 1;
   } else if (st.cur_b >= 0) {
-    st.flush(a, s_cum, W, v, lane);
+    end_pair = st.cur_b * a.hkv + st.cur_h;
+    const PairSpan ps = pair_span(a, s_cum, W, total, end_pair);
+    if (ps.vf == ps.vl) {
+      st.flush(a, s_cum, W, v, lane);  // covered alone: final output
+      end_pair = -1;
+    } else {
+      st.save(s_states + warp * kRec, a.group, lane);
+    }
   }
-
-  // ============ merge: the last CTA to finish a split pair combines it ============
-  __threadfence();
+  if (lane == 0) s_endpair[warp] = end_pair;
   consumer_barrier(kConsumers);
   if (s_abort) return;  // every consumer warp reads the same flag after the barrier
+  const int cta = blockIdx.x;
+  for (int w0 = 0; w0 < NCW;) {
+    const int p = s_endpair[w0];
+    int w1 = w0 + 1;
+    while (w1 < NCW && s_endpair[w1] == p) ++w1;
+    if (p >= 0) {
+      const PairSpan ps = pair_span(a, s_cum, W, total, p);
+      const int cf = ps.vf / NCW, cl = ps.vl / NCW;
+      if (cf == cl) {  // the whole pair is in this CTA
+        merge_sources<T, D, NCW>(a, p, s_states, w0, w1 - w0, 0, 0,
+                                 ps.last_continues ? ps.vl : -1, true, 0, s_scratch);
+      } else {
+        merge_sources<T, D, NCW>(a, p, s_states, w0, w1 - w0, 0, 0, -1, false, cta, s_scratch);
+      }
+    }
+    w0 = w1;
+  }
+  // (merge_sources ends with a barrier; the counter atomic below releases the
+  //  partials written by this CTA's threads, warp partials included)
   const int x0 = v0 * W, x1 = min((v0 + NCW) * W, total);
   const TilePos pf = locate(s_cum, a.batch, a.hkv, x0);
   const TilePos pl = locate(s_cum, a.batch, a.hkv, x1 - 1);
-  for (int p = pf.b * a.hkv + pf.h; p <= pl.b * a.hkv + pl.h; ++p) {
-    const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
-    const int tb = s_cum[b + 1] - s_cum[b];
-    if (tb == 0) continue;
-    const int stt = s_cum[b] * a.hkv + h * tb;
-    const int vf = stt / W, vl = (stt + tb - 1) / W;
-    if (vf == vl) continue;  // one worker covered it and wrote the output
-    if (threadIdx.x == 0) {
-      const int old = atomicAdd(a.counters + p, 1);
-      s_flag = (old == vl / NCW - vf / NCW) ? 1 : 0;
-      __threadfence();
+  const int p_first = pf.b * a.hkv + pf.h, p_last = pl.b * a.hkv + pl.h;
+  // Counter bumps for every split pair this CTA touched, all in flight at
+  // once; the pairs whose count this CTA completes become merge jobs.
+  MergeJob* s_jobs = reinterpret_cast<MergeJob*>(s_scratch);
+  __shared__ int s_njobs;
+  for (int base = p_first; base <= p_last; base += kConsumers) {
+    if (threadIdx.x == 0) s_njobs = 0;
+    consumer_barrier(kConsumers);
+    const int p = base + threadIdx.x;
+    if (p <= p_last) {
+      const PairSpan ps = pair_span(a, s_cum, W, total, p);
+      const int cf = ps.vf / NCW, cl = ps.vl / NCW;
+      if (ps.tiles > 0 && ps.vf != ps.vl && cf != cl) {
+        if (atomic_add_acq_rel_gpu(a.counters + p, 1) == cl - cf) {
+          const int vl_end = ps.last_continues ? ps.vl - 1 : ps.vl;
+          MergeJob job;
+          job.p = p;
+          job.c0 = ps.vf / NCW;
+          job.n_cta = vl_end / NCW - job.c0 + 1;
+          job.warp_slot = ps.last_continues ? ps.vl : -1;
+          s_jobs[atomicAdd(&s_njobs, 1)] = job;
+          a.counters[p] = 0;  // ready for the next call
+        }
+      }
     }
     consumer_barrier(kConsumers);
-    if (s_flag) {
-      merge_pair<T, D, NCW>(a, p, vf, vl, smem);
-      consumer_barrier(kConsumers);
-      if (threadIdx.x == 0) a.counters[p] = 0;  // ready for the next call
+    const int n_jobs = s_njobs;
+    if (n_jobs > 0) {
+      merge_global<T, D, NCW>(a, s_jobs, n_jobs);
+      // jobs with too many sources for the one-pass merge
+      for (int j = 0; j < n_jobs; ++j) {
+        const MergeJob job = s_jobs[j];
+        if (job.n_cta + (job.warp_slot >= 0 ? 1 : 0) > kMaxDirectSources)
+          merge_sources<T, D, NCW>(a, job.p, s_states, 0, 0, job.c0, job.n_cta, job.warp_slot,
+                                   true, 0, s_scratch + 4 * kConsumers);
+      }
     }
     consumer_barrier(kConsumers);
   }
@@ -711,15 +922,20 @@ int64_t paged_decode_slots(int batch, int num_kv_heads) {
 // counters (the first roundup(4*B*Hkv, 256) bytes) must be zero when a call
 // starts; a call that completes leaves them zero.
 struct WorkspaceLayout {
-  int64_t o_bytes, ml_bytes, cnt_bytes;
+  int64_t cnt_bytes, o_bytes, ml_bytes, cta_o_bytes, cta_ml_bytes;
   WorkspaceLayout(int batch, int hq, int hkv, int d) {
+    auto up = [](int64_t x) { return ((x + 255) / 256) * 256; };
     const int64_t group = hq / hkv;
-    const int64_t slots = paged_decode_slots(batch, hkv);
-    o_bytes = ((slots * group * d * 4 + 255) / 256) * 256;
-    ml_bytes = ((slots * group * 2 * 4 + 255) / 256) * 256;
-    cnt_bytes = ((static_cast<int64_t>(batch) * hkv * 4 + 255) / 256) * 256;
+    const int64_t pairs = static_cast<int64_t>(batch) * hkv;
+    const int64_t slots = paged_decode_slots(batch, hkv);            // warp partials
+    const int64_t cta_slots = num_sms_current_device() + pairs;      // CTA partials
+    cnt_bytes = up(pairs * 4);
+    o_bytes = up(slots * group * d * 4);
+    ml_bytes = up(slots * group * 2 * 4);
+    cta_o_bytes = up(cta_slots * group * d * 4);
+    cta_ml_bytes = up(cta_slots * group * 2 * 4);
   }
-  int64_t total() const { return o_bytes + ml_bytes + cnt_bytes; }
+  int64_t total() const { return cnt_bytes + o_bytes + ml_bytes + cta_o_bytes + cta_ml_bytes; }
 };
 
 }  // namespace helm
@@ -790,10 +1006,13 @@ extern "C" int helm_paged_decode_attention(
   a.out_sb = out_stride_b;
   a.out_sh = out_stride_h;
   a.lse = lse;
-  a.counters = static_cast<int*>(workspace);
-  a.part_o = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ws.cnt_bytes);
-  a.part_ml =
-      reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ws.cnt_bytes + ws.o_bytes);
+  uint8_t* wsp = static_cast<uint8_t*>(workspace);
+  a.counters = reinterpret_cast<int*>(wsp);
+  a.part_o = reinterpret_cast<float*>(wsp + ws.cnt_bytes);
+  a.part_ml = reinterpret_cast<float*>(wsp + ws.cnt_bytes + ws.o_bytes);
+  a.cta_o = reinterpret_cast<float*>(wsp + ws.cnt_bytes + ws.o_bytes + ws.ml_bytes);
+  a.cta_ml =
+      reinterpret_cast<float*>(wsp + ws.cnt_bytes + ws.o_bytes + ws.ml_bytes + ws.cta_o_bytes);
   a.batch = batch;
   a.hq = num_q_heads;
   a.hkv = num_kv_heads;
