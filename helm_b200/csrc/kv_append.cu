@@ -150,6 +150,29 @@ __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const Appe
   }
 }
 
+// Plain row write for shapes the fused kernel does not cover (fp32 pages, any
+// head_dim): element-wise copy of each token's K and V rows into the pool.
+template <typename E>
+__global__ void kv_scatter_rows_kernel(const AppendArgs a, int head_dim) {
+  const int tok = blockIdx.x;
+  const int64_t row = a.slot_rows[tok];
+  if (row < 0) return;
+  const int64_t slot = row / a.page_size, r_in = row - (row / a.page_size) * a.page_size;
+  if (slot >= a.pool_pages) {
+    if (threadIdx.x == 0) report_status(HELM_DEV_BAD_PAGE);
+    return;
+  }
+  const int64_t head_elems = static_cast<int64_t>(a.page_size) * head_dim;
+  E* pool = static_cast<E*>(a.pool);
+  for (int e = threadIdx.x; e < 2 * a.hkv * head_dim; e += blockDim.x) {
+    const int kv = e / (a.hkv * head_dim), rem = e - kv * a.hkv * head_dim;
+    const int h = rem / head_dim, d = rem - h * head_dim;
+    const E* src = kv == 0 ? static_cast<const E*>(a.k) + tok * a.k_st + h * a.k_sh
+                           : static_cast<const E*>(a.v) + tok * a.v_st + h * a.v_sh;
+    pool[((slot * 2 + kv) * a.hkv + h) * head_elems + r_in * head_dim + d] = src[d];
+  }
+}
+
 template <typename T>
 int launch_append(int head_dim, const AppendArgs& a, int n, cudaStream_t s) {
   switch (head_dim) {
@@ -188,7 +211,39 @@ extern "C" int helm_kv_append(const void* q, int64_t q_stride_t, int64_t q_strid
   if (q_out != nullptr && q == nullptr) return HELM_ERR_INVALID_ARGUMENT;
   if ((cos == nullptr) != (sin == nullptr)) return HELM_ERR_INVALID_ARGUMENT;
   if (slot_rows != nullptr && kv_pool == nullptr) return HELM_ERR_INVALID_ARGUMENT;
-  if (dtype != HELM_DTYPE_BF16 && dtype != HELM_DTYPE_FP16) return HELM_ERR_UNSUPPORTED;
+  const bool processing = q_out != nullptr || q_norm_w != nullptr || k_norm_w != nullptr ||
+                          cos != nullptr || k_out != nullptr || v_out != nullptr;
+  const bool fused_shape = (dtype == HELM_DTYPE_BF16 || dtype == HELM_DTYPE_FP16) &&
+                           (head_dim == 64 || head_dim == 128 || head_dim == 256);
+  if (!fused_shape) {
+    // plain page write of any dtype / head_dim; norm and RoPE need the fused shape
+    if (processing || slot_rows == nullptr || head_dim <= 0) return HELM_ERR_UNSUPPORTED;
+    if (dtype != HELM_DTYPE_FP32 && dtype != HELM_DTYPE_BF16 && dtype != HELM_DTYPE_FP16)
+      return HELM_ERR_UNSUPPORTED;
+    AppendArgs a{};
+    a.k = k;
+    a.k_st = k_stride_t;
+    a.k_sh = k_stride_h;
+    a.v = v;
+    a.v_st = v_stride_t;
+    a.v_sh = v_stride_h;
+    a.pool = kv_pool;
+    a.pool_pages = pool_pages;
+    a.slot_rows = slot_rows;
+    a.hkv = num_kv_heads;
+    a.page_size = page_size;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (dtype == HELM_DTYPE_FP32)
+      kv_scatter_rows_kernel<float><<<num_tokens, 128, 0, s>>>(a, head_dim);
+    else
+      kv_scatter_rows_kernel<uint16_t><<<num_tokens, 128, 0, s>>>(a, head_dim);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+      set_last_cuda_error(e);
+      return HELM_ERR_CUDA;
+    }
+    return HELM_OK;
+  }
   // Each lane moves D/32 contiguous elements: rows must be aligned to that.
   const int64_t vec = head_dim / 32;  // elements per lane
   auto bad = [&](const void* p, std::initializer_list<int64_t> strides) {

@@ -29,8 +29,9 @@ class PagePool:
     """One tier's slot storage: [capacity, 2, H, P, D] on `device`."""
 
     def __init__(self, device: torch.device, num_kv_heads: int, page_size: int, head_dim: int,
-                 dtype: torch.dtype, capacity: int = 0):
+                 dtype: torch.dtype, capacity: int = 0, allocator=None):
         self.device = device
+        self.allocator = allocator
         self.shape_tail = (2, num_kv_heads, page_size, head_dim)
         self.dtype = dtype
         self.storage: Optional[torch.Tensor] = None
@@ -147,7 +148,8 @@ class KVAllocator:
         pool = self._pools.get(key)
         if pool is None:
             pool = PagePool(device, self.num_kv_heads, self.page_size, self.head_dim, self.dtype,
-                            self._initial["cuda" if device.type == "cuda" else "cpu"])
+                            self._initial["cuda" if device.type == "cuda" else "cpu"],
+                            allocator=self)
             self._pools[key] = pool
         return pool
 
@@ -199,6 +201,7 @@ class KVAllocator:
                 self.reserve_batch(16, device)
             page = self.cpu_free_pool.pop()
             page.state = "CPU"
+        page.generation += 1  # content changes from here on (cold-page staging key)
         page.layer_id = -1
         page.start_token = 0
         page.used_tokens = 0

@@ -11,12 +11,12 @@ What is different underneath:
   * K/V rows are written by the native fused append kernel, tier moves are
     copy-engine transfers (runs of slots merged into one cudaMemcpyAsync);
   * attention over the pages is the native split-KV kernel, fed an int32 page
-    table; cold pages are staged into reserved HBM slots on the copy stream
-    (per-layer, one layer ahead when driven by _decode_batched) and the kernel
-    reads them from there;
+    table that every layer keeps up to date incrementally; cold pages are
+    staged into reserved HBM slots on the copy stream (one layer ahead when
+    driven by _decode_batched) and the kernel reads them from there;
   * placement (page ids, tiers, start/used tokens, eviction order, stats) is
-    bit-identical to the reference; the data movement that the reference does
-    page by page is issued in batches after the bookkeeping.
+    identical to the reference; the data movement that the reference does page
+    by page is issued in batches after the bookkeeping.
 
 Queries on the CPU are not served here: CPU stages keep HELM's own
 implementation.  K/V dtypes are bf16 and fp16; head_dim 64, 128 or 256.
@@ -30,7 +30,6 @@ from typing import List, Optional
 
 import numpy as np
 import torch
-import torch.nn.functional as F
 
 from .. import _capi
 
@@ -99,18 +98,54 @@ class KVPage:
     # pool slot and owning pool (set by KVAllocator; -1 / None for pages made by hand)
     slot: int = field(default=-1, compare=False)
     pool: Optional[object] = field(default=None, repr=False, compare=False)
+    # bumped whenever the allocator hands the page out again (content changes)
+    generation: int = field(default=0, repr=False, compare=False)
 
 
 class LayerKVCache:
+    """Ordered pages of one layer, plus the int32 page-table view of them that
+    the decode kernel consumes (kept in step by KVCacheManager)."""
+
     def __init__(self, layer_id: int):
         self.layer_id = layer_id
         self.pages: List[KVPage] = []
         self.tail_page: Optional[KVPage] = None
         self.total_tokens: int = 0
+        # slot of page i (>= 0: device pool; -1 - s: host-pool slot s), used tokens
+        self._slots = np.zeros(16, np.int32)
+        self._used = np.zeros(16, np.int32)
+        self._n = 0
+        self._ragged = False     # a page other than the last is not full
+        self._cold = 0           # pages on the host tier
 
     def append_page(self, page: KVPage):
         self.pages.append(page)
         self.tail_page = page
+
+    # -- page-table bookkeeping ------------------------------------------------
+    def _track_new(self, page: KVPage) -> None:
+        n = self._n
+        if n == len(self._slots):
+            self._slots = np.concatenate([self._slots, np.zeros_like(self._slots)])
+            self._used = np.concatenate([self._used, np.zeros_like(self._used)])
+        if n > 0 and self._used[n - 1] != page.capacity_tokens:
+            self._ragged = True
+        self._slots[n] = _slot_code(page)
+        self._used[n] = page.used_tokens
+        if page.state == "CPU":
+            self._cold += 1
+        self._n = n + 1
+
+    def _table_ok(self) -> bool:
+        """True when the incremental table describes `pages` (callers may have
+        edited the list directly; then the slow path rebuilds from the list)."""
+        return self._n == len(self.pages) and (self._n == 0 or self.pages[-1] is self.tail_page)
+
+
+def _slot_code(page: KVPage) -> int:
+    if page.pool is None or page.slot < 0:
+        return -(1 << 30)
+    return page.slot if not page.pool.is_host else -1 - page.slot
 
 
 # ── copy streams (kv_cache.py:378-396) ──────────────────────────────────────────
@@ -138,64 +173,70 @@ def _async_kv_prefetch_enabled() -> bool:
 class ColdPageStager:
     """Stages host-tier pages into reserved HBM slots of a device pool.
 
-    Two halves of staging slots alternate by layer parity, so the copy of
+    Two halves of staging slots alternate by layer parity, so the copies of
     layer l+1's cold pages (issued on the copy stream while layer l computes)
-    never overwrites what layer l's attention is reading.  Before a half is
-    refilled the copy stream waits for the event recorded after the last
-    kernel that read it.
+    never overwrite what layer l's attention reads.  Before a half is refilled
+    for another layer, the copy stream waits for the event recorded after the
+    last kernel that read it.  Within a half, pages already staged for the same
+    layer (same page id and generation) are not copied again.
     """
 
     def __init__(self, pool):
         self.pool = pool
         self.halves: list[list[int]] = [[], []]
-        self.released: list[Optional[torch.cuda.Event]] = [None, None]
-        self.ready: dict = {}  # key -> (page ids, slots, event, parity)
+        self.maps: list[dict] = [{}, {}]          # (page_id, generation) -> slot
+        self.owner: list = [None, None]           # layer key staged in the half
+        self.pending: list = [None, None]         # copy-completion events
+        self.released: list = [None, None]        # last-reader events
 
-    def _slots(self, parity: int, n: int) -> list[int]:
+    def _slot(self, parity: int, i: int) -> int:
         half = self.halves[parity]
-        while len(half) < n:
+        while len(half) <= i:
             self.pool.reserve_capacity(1)
             slot = self.pool.next_slot
             self.pool.next_slot += 1
             self.pool.staging.append(slot)
             half.append(slot)
-        return half[:n]
+        return half[i]
 
     def issue(self, key, parity: int, pages: list, device: torch.device) -> None:
-        """Starts the host->device copies of `pages` into half `parity`."""
-        ids = tuple(p.page_id for p in pages)
-        slots = self._slots(parity, len(pages))
+        """Starts host->device copies of the pages not yet staged in `parity`."""
+        if self.owner[parity] != key:
+            self.owner[parity] = key
+            self.maps[parity] = {}
+        m = self.maps[parity]
+        todo = [p for p in pages if (p.page_id, p.generation) not in m]
+        if not todo:
+            return
+        dst, src_by_pool = [], {}
+        for p in todo:
+            s = self._slot(parity, len(m))
+            m[(p.page_id, p.generation)] = s
+            src_by_pool.setdefault(id(p.pool), (p.pool, [], []))
+            src_by_pool[id(p.pool)][1].append(s)
+            src_by_pool[id(p.pool)][2].append(p.slot)
         compute = torch.cuda.current_stream(device)
-        use_side = _async_kv_prefetch_enabled()
-        stream = _get_kv_copy_stream(device) if use_side else compute
-        # pages evicted by this step's appends were queued on the compute stream
-        after_evictions = torch.cuda.Event()
-        after_evictions.record(compute)
-        with torch.cuda.stream(stream):
-            stream.wait_event(after_evictions)
+        stream = _get_kv_copy_stream(device) if _async_kv_prefetch_enabled() else compute
+        if stream is not compute:
+            queued = torch.cuda.Event()     # evictions queued so far on the compute stream
+            queued.record(compute)
+            stream.wait_event(queued)
             if self.released[parity] is not None:
                 stream.wait_event(self.released[parity])
-            by_pool: dict = {}
-            for p, s in zip(pages, slots):
-                by_pool.setdefault(id(p.pool), (p.pool, [], []))
-                by_pool[id(p.pool)][1].append(s)
-                by_pool[id(p.pool)][2].append(p.slot)
-            for src_pool, dsts, srcs in by_pool.values():
-                _capi.copy_pages(self.pool.storage, src_pool.storage, dsts, srcs, device,
-                                 stream=stream)
-            ev = torch.cuda.Event()
-            ev.record(stream)
-        self.ready[key] = (ids, slots, ev, parity)
+        for src_pool, dsts, srcs in src_by_pool.values():
+            _capi.copy_pages(self.pool.storage, src_pool.storage, dsts, srcs, device,
+                             stream=stream)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.pending[parity] = ev
 
-    def take(self, key, parity: int, pages: list, device: torch.device) -> list[int]:
-        """Slots holding `pages` for the next kernel on the compute stream."""
-        ids = tuple(p.page_id for p in pages)
-        entry = self.ready.pop(key, None)
-        if entry is None or entry[0] != ids or entry[3] != parity:
-            self.issue(key, parity, pages, device)
-            entry = self.ready.pop(key)
-        torch.cuda.current_stream(device).wait_event(entry[2])
-        return entry[1]
+    def take(self, key, parity: int, pages: list, device: torch.device) -> list:
+        """Slots holding `pages`, ready for the next kernel on the compute stream."""
+        self.issue(key, parity, pages, device)
+        if self.pending[parity] is not None:
+            torch.cuda.current_stream(device).wait_event(self.pending[parity])
+        m = self.maps[parity]
+        return [m[(p.page_id, p.generation)] for p in pages]
 
     def release(self, parity: int, device: torch.device) -> None:
         ev = torch.cuda.Event()
@@ -203,14 +244,10 @@ class ColdPageStager:
         self.released[parity] = ev
 
 
-_stagers: dict = {}
-
-
 def _stager_for(pool) -> ColdPageStager:
-    st = _stagers.get(id(pool))
-    if st is None or st.pool is not pool:
-        st = ColdPageStager(pool)
-        _stagers[id(pool)] = st
+    st = getattr(pool, "_stager", None)
+    if st is None:
+        st = pool._stager = ColdPageStager(pool)
     return st
 
 
@@ -230,165 +267,171 @@ def _page_bytes_used(p: KVPage) -> int:
     return p.k_tensor[:, :, :p.used_tokens, :].numel() * p.k_tensor.element_size() * 2
 
 
-def _attend_lists(query: torch.Tensor, lists: list, scale: float,
-                  mask2d: Optional[torch.Tensor], softcap: Optional[float],
-                  lse: Optional[torch.Tensor] = None, stage_key=None,
-                  prefetch_next=None) -> torch.Tensor:
-    """Decode attention: query [B, Hq, D]; lists[b] = active pages of sequence b
-    (lists may be one shared list for all b).  Returns out [B, Hq, D]."""
-    dev = query.device
-    B = query.shape[0]
-    shared = len(lists) == 1 and B > 1
-    seqs = lists if not shared else lists[:1]
-    all_pages = [p for pages in seqs for p in pages]
-    if not all_pages:
-        out = torch.zeros_like(query)
-        if lse is not None:
-            lse.fill_(-math.inf)
-        return out
-    Hkv = all_pages[0].k_tensor.shape[1]
-    # Pool path: every page lives in this device's pool or in a host pool of
-    # the same geometry.  Otherwise the pages are copied into a scratch pool.
-    dev_pool = None
-    for p in all_pages:
-        if p.pool is not None and not p.pool.is_host and p.pool.device == dev:
-            dev_pool = p.pool
-            break
-    if dev_pool is None:
-        for p in all_pages:
-            if p.pool is not None and p.pool.is_host:
-                alloc_pool = _device_pool_like(p.pool, dev)
-                if alloc_pool is not None:
-                    dev_pool = alloc_pool
-                break
-    pool_ok = dev_pool is not None and all(
-        p.pool is not None and p.pool.shape_tail == dev_pool.shape_tail
-        and p.pool.dtype == query.dtype and (p.pool is dev_pool or p.pool.is_host)
-        for p in all_pages)
-    if not pool_ok:
-        return _attend_foreign(query, seqs, shared, scale, mask2d, softcap, lse)
+class _Tables:
+    """Page table of several sequences in pool-slot form, before staging."""
 
-    P = dev_pool.shape_tail[2]
-    nseq = len(seqs)
-    maxp = max(len(s) for s in seqs)
-    table = np.zeros((nseq, maxp), np.int32)
+    def __init__(self, slots: np.ndarray, used: np.ndarray, nump: np.ndarray, ragged: bool,
+                 cold: list, cold_pos: list):
+        self.slots, self.used, self.nump, self.ragged = slots, used, nump, ragged
+        self.cold, self.cold_pos = cold, cold_pos   # [(item, [pages])], [(item, idx array)]
+
+
+def _tables_from_lists(lists: list, dev_pool) -> Optional[_Tables]:
+    """Slow path: build the table from page objects.  None if some page is
+    not a slot of `dev_pool` or of a host pool of the same allocator."""
+    nseq = len(lists)
+    maxp = max(1, max(len(s) for s in lists))
+    slots = np.zeros((nseq, maxp), np.int32)
     used = np.zeros((nseq, maxp), np.int32)
-    cold, cold_pos = [], []
+    nump = np.array([len(s) for s in lists], np.int32)
+    P = dev_pool.shape_tail[2]
     ragged = False
-    for b, pages in enumerate(seqs):
+    cold, cold_pos = [], []
+    for b, pages in enumerate(lists):
+        cp, ci = [], []
         for i, p in enumerate(pages):
-            used[b, i] = p.used_tokens
+            if p.pool is None or p.pool.shape_tail != dev_pool.shape_tail or \
+                    p.pool.dtype != dev_pool.dtype:
+                return None
             if p.pool is dev_pool:
-                table[b, i] = p.slot
+                slots[b, i] = p.slot
+            elif p.pool.is_host and p.pool.allocator is dev_pool.allocator:
+                cp.append(p)
+                ci.append(i)
             else:
-                cold.append(p)
-                cold_pos.append((b, i))
+                return None
+            used[b, i] = p.used_tokens
             if p.used_tokens != P and i != len(pages) - 1:
                 ragged = True
-    if cold:
-        _record_prefetch(len(cold), sum(_page_bytes_used(p) for p in cold))
-        stager = _stager_for(dev_pool)
-        parity = 0 if stage_key is None else (stage_key[-1] & 1)
-        slots = stager.take(stage_key, parity, cold, dev)
-        for (b, i), s in zip(cold_pos, slots):
-            table[b, i] = s
-    out = _launch(query, dev_pool, table, used, ragged, shared, scale, mask2d, softcap, lse)
-    if cold:
-        stager.release(parity, dev)
-    if prefetch_next is not None:
-        prefetch_next(dev_pool)
-    return out
+        if cp:
+            cold.append((b, cp))
+            cold_pos.append((b, np.array(ci, np.int64)))
+    return _Tables(slots, used, nump, ragged, cold, cold_pos)
 
 
-def _device_pool_like(host_pool, dev):
-    """The device pool of the allocator that owns `host_pool` (pages of one
-    allocator share geometry), if it exists already."""
-    for p in list(host_pool.pages.values())[:1]:
-        alloc = getattr(p, "_allocator", None)
-        if alloc is not None:
-            return alloc.pool_for(dev)
-    return _ALLOCATOR_POOLS.get((id(host_pool), dev.index))
-
-
-_ALLOCATOR_POOLS: dict = {}
-
-
-def _launch(query, pool, table, used, ragged, shared, scale, mask2d, softcap, lse):
+def _run_kernel(query: torch.Tensor, pool, t: _Tables, scale, mask2d, softcap, lse,
+                shared: bool = False):
+    """Copies the table to the device (one pinned transfer) and launches."""
     dev = query.device
     B = query.shape[0]
-    nseq = table.shape[0]
-    lens = used.sum(axis=1).astype(np.int32)
-    parts = [lens, table.reshape(-1)]
-    if ragged:
-        start = np.zeros_like(used)
-        if used.shape[1] > 1:
-            start[:, 1:] = np.cumsum(used, axis=1)[:, :-1]
-        nump = np.array([int((used[b] > 0).sum()) if False else used.shape[1] for b in range(nseq)],
-                        np.int32)
-        parts += [nump, used.reshape(-1), start.reshape(-1)]
+    nseq, maxp = t.slots.shape
+    lens = t.used.sum(axis=1).astype(np.int32)
+    parts = [lens, t.slots.reshape(-1)]
+    if t.ragged:
+        start = np.zeros_like(t.used)
+        if maxp > 1:
+            start[:, 1:] = np.cumsum(t.used, axis=1)[:, :-1]
+        parts += [t.nump, t.used.reshape(-1), start.reshape(-1)]
     host = torch.from_numpy(np.concatenate(parts).astype(np.int32)).pin_memory()
     blob = host.to(dev, non_blocking=True)
-    maxp = table.shape[1]
     kl = blob[:nseq]
     pt = blob[nseq:nseq + nseq * maxp].view(nseq, maxp)
     kw = {}
-    if ragged:
+    if t.ragged:
         o = nseq + nseq * maxp
-        kw = dict(num_pages=blob[o:o + nseq], page_used=blob[o + nseq:o + nseq + nseq * maxp].view(nseq, maxp),
+        kw = dict(num_pages=blob[o:o + nseq],
+                  page_used=blob[o + nseq:o + nseq + nseq * maxp].view(nseq, maxp),
                   page_start=blob[o + nseq + nseq * maxp:].view(nseq, maxp))
-    if shared:  # every batch row attends to the same pages
-        pt = pt.expand(B, maxp)
-        kl = kl.expand(B)
-        if ragged:
-            kw = {k: (v.expand(B) if v.dim() == 1 else v.expand(B, maxp)) for k, v in kw.items()}
-        pt, kl = pt.contiguous(), kl.contiguous()
-        kw = {k: v.contiguous() for k, v in kw.items()}
+    if shared and B > 1:  # every batch row attends to the same pages
+        pt = pt.expand(B, maxp).contiguous()
+        kl = kl.expand(B).contiguous()
+        kw = {k: (v.expand(B) if v.dim() == 1 else v.expand(B, maxp)).contiguous()
+              for k, v in kw.items()}
     q3 = query if query.stride(-1) == 1 else query.contiguous()
     out, _ = _capi.paged_decode_attention(
-        q3, pool.storage, pt, kl, num_kv_heads=pool.shape_tail[1], page_size=pool.shape_tail[2],
-        scale=scale, softcap=softcap, mask=mask2d, lse=lse,
+        q3, pool.storage, pt, kl, num_kv_heads=pool.shape_tail[1],
+        page_size=pool.shape_tail[2], scale=scale, softcap=softcap, mask=mask2d, lse=lse,
         max_kv_len_hint=int(lens.max()) if lens.size else 0, **kw)
     return out
 
 
-def _attend_foreign(query, seqs, shared, scale, mask2d, softcap, lse):
-    """Pages that are not pool slots (made by hand): copied into a scratch pool."""
+def _stage_and_run(query, dev_pool, t: _Tables, scale, mask2d, softcap, lse=None,
+                   stage_key=None, parity: int = 0, shared: bool = False, record=True):
+    """Stages cold pages (if any) and runs the kernel."""
     dev = query.device
+    stager = None
+    if t.cold:
+        stager = _stager_for(dev_pool)
+        flat = [p for _, pages in t.cold for p in pages]
+        if record:
+            for _, pages in t.cold:
+                _record_prefetch(len(pages), sum(_page_bytes_used(p) for p in pages))
+        staged = stager.take(stage_key, parity, flat, dev)
+        k = 0
+        for b, idx in t.cold_pos:
+            t.slots[b, idx] = staged[k:k + len(idx)]
+            k += len(idx)
+    out = _run_kernel(query, dev_pool, t, scale, mask2d, softcap, lse, shared=shared)
+    if stager is not None:
+        stager.release(parity, dev)
+    return out
+
+
+def _attend_lists(query: torch.Tensor, lists: list, scale: float,
+                  mask2d: Optional[torch.Tensor], softcap: Optional[float],
+                  lse: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode attention: query [B, Hq, D]; lists[b] = active pages of sequence b
+    (or one list shared by every b).  Returns out [B, Hq, D]."""
     B = query.shape[0]
-    Hkv, D = seqs[0][0].k_tensor.shape[1], seqs[0][0].k_tensor.shape[3]
-    Pt = max(p.used_tokens for s in seqs for p in s)
-    n = sum(len(s) for s in seqs)
+    shared = len(lists) == 1 and B > 1
+    all_pages = [p for pages in lists for p in pages]
+    if not all_pages:
+        if lse is not None:
+            lse.fill_(-math.inf)
+        return torch.zeros_like(query)
+    dev_pool = None
+    for p in all_pages:
+        if p.pool is not None and p.pool.allocator is not None:
+            dev_pool = p.pool.allocator.pool_for(query.device)
+            break
+    t = _tables_from_lists(lists, dev_pool) if dev_pool is not None else None
+    if t is None:
+        return _attend_foreign(query, lists, shared, scale, mask2d, softcap, lse)
+    if dev_pool.storage is None:
+        dev_pool.reserve_capacity(1)
+    return _stage_and_run(query, dev_pool, t, scale, mask2d, softcap, lse,
+                          stage_key=("direct", id(lists)), parity=0, shared=shared)
+
+
+class _ScratchPool:
+    """Page pool made for pages that are not slots of an allocator pool."""
+
+    def __init__(self, storage):
+        self.storage = storage
+        self.shape_tail = tuple(storage.shape[1:])
+
+
+def _attend_foreign(query, lists, shared, scale, mask2d, softcap, lse):
+    """Pages made by hand (any tensors): copied into a scratch pool first."""
+    dev = query.device
+    p0 = lists[0][0]
+    Hkv, D = p0.k_tensor.shape[1], p0.k_tensor.shape[3]
+    Pt = max(p.used_tokens for s in lists for p in s)
+    n = sum(len(s) for s in lists)
     scratch = torch.empty(n, 2, Hkv, Pt, D, dtype=query.dtype, device=dev)
-    maxp = max(len(s) for s in seqs)
-    table = np.zeros((len(seqs), maxp), np.int32)
-    used = np.zeros((len(seqs), maxp), np.int32)
+    maxp = max(len(s) for s in lists)
+    slots = np.zeros((len(lists), maxp), np.int32)
+    used = np.zeros((len(lists), maxp), np.int32)
     k = 0
     cpu_pages = []
-    for b, pages in enumerate(seqs):
+    for b, pages in enumerate(lists):
         for i, p in enumerate(pages):
             u = p.used_tokens
             scratch[k, 0, :, :u].copy_(p.k_tensor[0, :, :u], non_blocking=True)
             scratch[k, 1, :, :u].copy_(p.v_tensor[0, :, :u], non_blocking=True)
             if p.k_tensor.device.type != "cuda":
                 cpu_pages.append(p)
-            table[b, i] = k
+            slots[b, i] = k
             used[b, i] = u
             k += 1
     if cpu_pages:
         _record_prefetch(len(cpu_pages), sum(_page_bytes_used(p) for p in cpu_pages))
-
-    class _Scratch:
-        storage = scratch
-        shape_tail = tuple(scratch.shape[1:])
-
-    ragged = bool(np.any((used != Pt) & (np.arange(maxp)[None, :] <
-                                        np.array([len(s) for s in seqs])[:, None] - 1)))
-    return _launch(query, _Scratch, table, used, True or ragged, shared, scale, mask2d, softcap,
-                   lse)
+    t = _Tables(slots, used, np.array([len(s) for s in lists], np.int32), True, [], [])
+    return _run_kernel(query, _ScratchPool(scratch), t, scale, mask2d, softcap, lse, shared)
 
 
-def _mask_2d(attention_mask: Optional[torch.Tensor], B: int, T: int, dev) -> Optional[torch.Tensor]:
-    """[B|1, 1, 1, >=T] additive mask -> [B|1, T] view (dtype kept)."""
+def _mask_2d(attention_mask: Optional[torch.Tensor], T: int, dev) -> Optional[torch.Tensor]:
+    """[B|1, 1, q, >=T] additive mask -> [B|1, T] (last query row; dtype kept)."""
     if attention_mask is None:
         return None
     m = attention_mask
@@ -398,6 +441,10 @@ def _mask_2d(attention_mask: Optional[torch.Tensor], B: int, T: int, dev) -> Opt
         m = m[:, :T]
     else:
         raise ValueError(f"unsupported attention_mask shape {tuple(attention_mask.shape)}")
+    if m.shape[-1] < T:  # the kernel indexes the mask by token position
+        raise ValueError(f"attention_mask covers {m.shape[-1]} keys, the cache holds {T}")
+    if m.stride(-1) != 1:
+        m = m.contiguous()
     if m.device != dev:
         m = m.to(dev)
     if m.dtype not in (torch.float32, torch.bfloat16, torch.float16):
@@ -415,7 +462,8 @@ def perform_streaming_attention(query: torch.Tensor, pages: List[KVPage], scale:
     fp32 and returned in the query dtype.  No active page -> zeros.
 
     q_len == 1 runs the native split-KV decode kernel.  q_len > 1 (a prefill
-    chunk over cached pages) gathers the pages and calls the library SDPA.
+    chunk over cached pages) gathers the pages and runs the fp32 math with the
+    library matmul/softmax.
     """
     active = [p for p in pages if p.used_tokens > 0 and p.state != "DEAD"]
     if scale is None:
@@ -426,18 +474,20 @@ def perform_streaming_attention(query: torch.Tensor, pages: List[KVPage], scale:
     B, Hq, q_len, D = query.shape
     T = sum(p.used_tokens for p in active)
     if q_len == 1:
-        mask2d = _mask_2d(attention_mask, B, T, query.device)
+        mask2d = _mask_2d(attention_mask, T, query.device)
         out = _attend_lists(query[:, :, 0, :], [active], scale, mask2d, softcap)
         return out.unsqueeze(2)
     return _prefill_over_pages(query, [active], scale, attention_mask, softcap)
 
 
 def _prefill_over_pages(query, lists, scale, attention_mask, softcap):
-    """q_len > 1 over cached pages: dense K/V from the pages, fp32 SDPA."""
+    """q_len > 1 over cached pages: dense K/V from the pages, fp32 math."""
     dev = query.device
-    cpu = [p for ps in lists for p in ps if p.k_tensor.device.type != "cuda"]
-    if cpu:
-        _record_prefetch(len(cpu), sum(_page_bytes_used(p) for p in cpu))
+    if any(p.k_tensor.device.type != "cuda" for ps in lists for p in ps):
+        for ps in lists:
+            cpu = [p for p in ps if p.k_tensor.device.type != "cuda"]
+            if cpu:
+                _record_prefetch(len(cpu), sum(_page_bytes_used(p) for p in cpu))
     outs = []
     for b in range(query.shape[0]):
         pages = lists[b] if len(lists) > 1 else lists[0]
@@ -469,7 +519,8 @@ class KVCacheManager:
     Extra keyword (not in the reference): sync_evictions (default True) makes
     every eviction finish before the call returns, as the reference's
     synchronous move does, so host code may read evicted pages at once.  With
-    False the device->host copies stay queued on the current stream.
+    False the device->host copies stay queued on the current stream and later
+    kernels and prefetches are ordered after them by the stream.
     """
 
     def __init__(self, allocator, gpu_high_watermark_bytes: int = 512 * 1024 * 1024, *,
@@ -478,6 +529,7 @@ class KVCacheManager:
         self.layers: dict = {}
         self.gpu_high_watermark_bytes = gpu_high_watermark_bytes
         self.sync_evictions = sync_evictions
+        self._evicted = False
         self.cont_K: dict = {}
         self.cont_V: dict = {}
         self.cont_capacity: int = 0
@@ -501,8 +553,15 @@ class KVCacheManager:
         page.layer_id = layer_id
         page.start_token = layer.total_tokens
         page.used_tokens = used
+        if not layer._table_ok():
+            _rebuild_table(layer)
         layer.append_page(page)
+        layer._track_new(page)
         return page
+
+    def _begin(self):
+        if self.allocator._deferred is None:
+            self.allocator._deferred = []
 
     def append_prefill(self, layer_id: int, K_prefill: torch.Tensor, V_prefill: torch.Tensor):
         """Appends a [1, H, S, D] chunk in page-size pieces, enforcing residency
@@ -512,72 +571,79 @@ class KVCacheManager:
         P = self.allocator.page_size
         device = K_prefill.device
         placed = []
-        self.allocator._deferred = []
+        self._begin()
         try:
             for start in range(0, seq_len, P):
                 n = min(P, seq_len - start)
                 page = self._new_page(layer, layer_id, device, n)
-                placed.append((page, start, n))
+                placed.append((page, page.pool, page.slot, start, n, 0))
                 layer.total_tokens += n
                 self._enforce_residency_policy()
             self._write_rows(placed, K_prefill, V_prefill)
         finally:
-            self._finish_appends(device)
+            self._finish(device)
 
     def append_decode(self, layer_id: int, K_new: torch.Tensor, V_new: torch.Tensor,
                       skip_residency: bool = False):
         """Appends one token [1, H, 1, D] to the tail page (kv_cache.py:145-171)."""
         device = K_new.device
-        self.allocator._deferred = []
+        self._begin()
         try:
-            page, idx = self._reserve_decode_row(layer_id, device)
+            place = self._reserve_decode_row(layer_id, device)
             if not skip_residency:
                 self._enforce_residency_policy()
-            self._write_rows([(page, 0, 1)], K_new, V_new, dst_row0=idx)
+            self._write_rows([place], K_new, V_new)
         finally:
-            self._finish_appends(device)
+            self._finish(device)
 
     def _reserve_decode_row(self, layer_id: int, device):
+        """Bookkeeping of one decode append; returns the row placement."""
         layer = self._layer(layer_id)
         if layer.tail_page is None or layer.tail_page.used_tokens == layer.tail_page.capacity_tokens:
             self._new_page(layer, layer_id, device, 0)
+        elif not layer._table_ok():
+            _rebuild_table(layer)
         page = layer.tail_page
         idx = page.used_tokens
         page.used_tokens += 1
         layer.total_tokens += 1
-        return page, idx
+        layer._used[layer._n - 1] = page.used_tokens
+        return (page, page.pool, page.slot, 0, 1, idx)
 
-    def _write_rows(self, placed, K, V, dst_row0: int = 0):
-        """Writes K/V rows [1, H, S, D]: placed = [(page, src_start, n)], each
-        page receiving rows dst_row0.. (prefill pages start at row 0)."""
+    def _write_rows(self, placed, K, V):
+        """Writes K/V rows [1, H, S, D]; placed = [(page, pool, slot, src_start,
+        n, dst_row0)] captured when the pages were placed (a page may have been
+        evicted since: its data is written to the old slot, which the deferred
+        device->host copy reads afterwards)."""
         if not placed:
             return
         if K.device.type != "cuda":
-            for page, s, n in placed:
-                page.k_tensor[:, :, dst_row0:dst_row0 + n, :].copy_(K[:, :, s:s + n, :])
-                page.v_tensor[:, :, dst_row0:dst_row0 + n, :].copy_(V[:, :, s:s + n, :])
+            for page, pool, slot, s, n, r0 in placed:
+                pool.storage[slot, 0, :, r0:r0 + n, :].copy_(K[0, :, s:s + n, :])
+                pool.storage[slot, 1, :, r0:r0 + n, :].copy_(V[0, :, s:s + n, :])
             return
         P = self.allocator.page_size
-        rows = []
-        for page, s, n in placed:
-            base = page.slot * P + dst_row0
-            rows.extend(range(base, base + n))
-        pool = placed[0][0].pool
-        rows_t = torch.tensor(rows, dtype=torch.int64).pin_memory().to(K.device, non_blocking=True)
+        pool = placed[0][1]
+        rows = np.empty(sum(x[4] for x in placed), np.int64)
+        k = 0
+        for page, pl, slot, s, n, r0 in placed:
+            if pl is not pool:
+                raise RuntimeError("rows of one append must land in one pool")
+            rows[k:k + n] = np.arange(slot * P + r0, slot * P + r0 + n)
+            k += n
+        rows_t = torch.from_numpy(rows).pin_memory().to(K.device, non_blocking=True)
         kt = K[0].transpose(0, 1)  # [S, H, D]
         vt = V[0].transpose(0, 1)
         if kt.dtype != pool.dtype:
             kt, vt = kt.to(pool.dtype), vt.to(pool.dtype)
         _capi.kv_append(k=kt, v=vt, pool=pool.storage, slot_rows=rows_t, page_size=P)
 
-    def _finish_appends(self, device):
+    def _finish(self, device):
+        """Issues deferred evictions; waits for them when sync_evictions."""
         self.allocator.flush_deferred()
-        if self.sync_evictions and self._evicted_since_sync:
-            if torch.device(device).type == "cuda":
-                torch.cuda.current_stream(device).synchronize()
-        self._evicted_since_sync = False
-
-    _evicted_since_sync = False
+        if self.sync_evictions and self._evicted and torch.device(device).type == "cuda":
+            torch.cuda.current_stream(device).synchronize()
+        self._evicted = False
 
     def iterate_layer_pages(self, layer_id: int):
         if layer_id not in self.layers:
@@ -603,31 +669,34 @@ class KVCacheManager:
         gpu_pages.sort(key=lambda t: t[1].start_token)
         evicted_bytes = 0
         n_moved = 0
-        deferred_outside = self.allocator._deferred is None
+        direct = self.allocator._deferred is None
         dev = None
         for layer, page in gpu_pages:
             if evicted_bytes >= bytes_to_evict:
                 break
             original_start = page.start_token
             dev = page.device
+            table_ok = layer._table_ok()
             new_page = self.allocator.move_page(page, torch.device("cpu"))
             assert new_page.start_token == original_start, "Page invariant broken during migration"
             idx = next(i for i, p in enumerate(layer.pages) if p is page)
             layer.pages[idx] = new_page
             if layer.tail_page is page:
                 layer.tail_page = new_page
+            if table_ok:
+                layer._slots[idx] = _slot_code(new_page)
+                layer._cold += 1
             evicted_bytes += new_page.k_tensor.numel() * new_page.k_tensor.element_size() * 2
             n_moved += 1
         if n_moved:
-            self._evicted_since_sync = True
-            if deferred_outside and self.sync_evictions and dev is not None:
+            self._evicted = True
+            if direct and self.sync_evictions and dev is not None:
                 torch.cuda.current_stream(dev).synchronize()
-                self._evicted_since_sync = False
+                self._evicted = False
         _record_eviction(n_moved, evicted_bytes)
 
     def _enforce_residency_policy(self):
-        bpp = self.allocator.bytes_per_page
-        gpu_bytes = bpp * len(self._evictable())
+        gpu_bytes = self.allocator.bytes_per_page * len(self._evictable())
         if gpu_bytes > self.gpu_high_watermark_bytes:
             self.evict_pages(gpu_bytes - self.gpu_high_watermark_bytes)
 
@@ -648,6 +717,7 @@ class KVCacheManager:
             layer.pages.clear()
             layer.tail_page = None
             layer.total_tokens = 0
+            _rebuild_table(layer)
         self.layers.clear()
 
     def all_gpu_resident(self, layer_id: int) -> bool:
@@ -660,7 +730,8 @@ class KVCacheManager:
 
     # -- contiguous buffers (kv_cache.py:269-354) --------------------------------
     # The paged kernel reads pages at full bandwidth, so the decode path here
-    # always uses pages; these buffers are kept for API compatibility.
+    # always appends to and reads from pages; these buffers are kept for API
+    # compatibility only.
     def build_contiguous(self, num_layers: int, num_kv_heads: int, head_dim: int,
                          capacity: int, device: torch.device, dtype: torch.dtype) -> bool:
         cap = capacity
@@ -713,7 +784,8 @@ class KVCacheManager:
         s, e = self.cont_prefill_len, self.cont_seq_len
         if e > s:
             for lid in range(self.cont_num_layers):
-                self.append_prefill(lid, self.cont_K[lid][:, :, s:e, :], self.cont_V[lid][:, :, s:e, :])
+                self.append_prefill(lid, self.cont_K[lid][:, :, s:e, :],
+                                    self.cont_V[lid][:, :, s:e, :])
         self.drop_contiguous()
 
     def drop_contiguous(self):
@@ -743,3 +815,68 @@ class KVCacheManager:
                 elif page.state == "CPU":
                     cpu_bytes += page_bytes
         return {"gpu_active_bytes": gpu_bytes, "cpu_active_bytes": cpu_bytes}
+
+
+def _rebuild_table(layer: LayerKVCache) -> None:
+    """Re-derives a layer's page-table arrays from its page list."""
+    layer._slots = np.zeros(max(16, 2 * len(layer.pages)), np.int32)
+    layer._used = np.zeros_like(layer._slots)
+    layer._n = 0
+    layer._ragged = False
+    layer._cold = 0
+    tail, pages = layer.tail_page, list(layer.pages)
+    for p in pages:
+        layer._track_new(p)
+    layer.tail_page = tail
+
+
+def _layer_tables(kvcms: list, layer_id: int, dev_pool) -> Optional[_Tables]:
+    """Page table of one layer over several sequences from the incremental
+    per-layer arrays (no per-page Python work except for cold pages)."""
+    layers = []
+    for kvcm in kvcms:
+        layer = kvcm.layers.get(layer_id)
+        if layer is not None and not layer._table_ok():
+            _rebuild_table(layer)
+        layers.append(layer)
+    maxp = max(1, max((L._n for L in layers if L is not None), default=1))
+    nseq = len(kvcms)
+    slots = np.zeros((nseq, maxp), np.int32)
+    used = np.zeros((nseq, maxp), np.int32)
+    nump = np.zeros(nseq, np.int32)
+    ragged = False
+    cold, cold_pos = [], []
+    for b, L in enumerate(layers):
+        if L is None or L._n == 0:
+            continue
+        n = L._n
+        nump[b] = n
+        slots[b, :n] = L._slots[:n]
+        used[b, :n] = L._used[:n]
+        if L._ragged or np.any(L._used[:n] == 0):
+            ragged = True
+        if L._cold:
+            idx = np.nonzero(L._slots[:n] < 0)[0]
+            if np.any(L._slots[idx] == -(1 << 30)):
+                return None
+            cold.append((b, [L.pages[i] for i in idx]))
+            cold_pos.append((b, idx))
+    if ragged:
+        # pages with no tokens are dropped from the ragged lists
+        keep = used > 0
+        if not keep.all():
+            for b in range(nseq):
+                k = keep[b, :nump[b]]
+                if k.all():
+                    continue
+                sel = np.nonzero(k)[0]
+                remap = -np.ones(maxp, np.int64)
+                remap[sel] = np.arange(sel.size)
+                slots[b, :sel.size] = slots[b, sel]
+                used[b, :sel.size] = used[b, sel]
+                used[b, sel.size:] = 0
+                nump[b] = sel.size
+                for ci, (cb, idx) in enumerate(cold_pos):
+                    if cb == b:
+                        cold_pos[ci] = (b, remap[idx])
+    return _Tables(slots, used, nump, ragged, cold, cold_pos)

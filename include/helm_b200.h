@@ -161,6 +161,8 @@ int helm_paged_decode_attention_noalloc(const void* q, int64_t q_stride_b, int64
  *               token stride rope_stride_t
  *  q_out        [N, Hq, D], strides q_out_stride_t, q_out_stride_h (may be NULL)
  *  k_out, v_out optional copies of the processed K/V rows ([N, Hkv, D] dense)
+ * Norm, RoPE and q/k/v outputs need bf16/fp16 and head_dim 64, 128 or 256; a
+ * plain page write (all of them NULL) also takes fp32 and any head_dim.
  */
 int helm_kv_append(const void* q, int64_t q_stride_t, int64_t q_stride_h, const void* k,
                    int64_t k_stride_t, int64_t k_stride_h, const void* v, int64_t v_stride_t,
