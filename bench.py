@@ -321,12 +321,92 @@ def run_b200(args, rank: int, world: int, dev: torch.device):
     print(json.dumps(line), flush=True)
 
 
+def run_seqsplit(args, rank: int, world: int, dev: torch.device):
+    """Decode attention of BASELINE configs[3] at 131072 tokens (Qwen3-14B heads:
+    40 q / 8 KV, D=128, 16-token pages, B=1), the sequence split over `world`
+    GPUs: every rank streams its own page range from its own HBM, the fp32
+    partial states are all-gathered over NCCL and merged.  Total work is
+    fixed (strong scaling); time = max over ranks; value = algorithmic bytes of
+    the whole attention / time."""
+    from helm_b200.runtime.seq_parallel import SeqSplitAttention, split_ranges
+    from helm_b200 import _capi
+    Bq, Hq, Hkv, Dh, Pg, Tt = 1, 40, 8, 128, 16, 131072
+    kv_bytes = Bq * Tt * Hkv * Dh * 2 * 2
+    alg = kv_bytes + Bq * Hq * Dh * 2 * 2 + Bq * Hq * 4 + Bq * (Tt // Pg) * 4
+    a, b = split_ranges(Tt, Pg, world)[rank]
+    npg = -(-(b - a) // Pg)
+    g = torch.Generator().manual_seed(1000 + rank)
+    pool = torch.randn(npg + 8, 2, Hkv, Pg, Dh, generator=g).to(torch.bfloat16).to(dev)
+    pt = torch.randperm(npg + 8, generator=g)[:npg].view(1, npg).to(torch.int32).to(dev)
+    kl = torch.tensor([b - a], dtype=torch.int32, device=dev)
+    q = torch.randn(Bq, Hq, Dh, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(dev)
+    sp = SeqSplitAttention()
+
+    def step():
+        return sp.decode(q, pool, pt, kl, num_kv_heads=Hkv, page_size=Pg, scale=Dh ** -0.5,
+                         max_kv_len_hint=b - a)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    # the decode step (kernel, NCCL all-gather, merge) is replayed as one CUDA
+    # graph: no host work between steps
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        step()
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(dev)
+    with ClockSampler(dev.index) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    del graph  # graphs holding NCCL calls go before the process group
+    if _capi.device_status(dev) != 0:
+        raise RuntimeError("device status reported an error")
+    if rank == 0:
+        line = {"metric": METRIC, "value": alg / (ms / 1e3) / 1e9, "unit": "GB/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": "seqsplit128k: configs[3] attention, B=1, 40q/8kv, D=128, "
+                                       "T=131072, 16-token pages, split over the GPUs, NCCL "
+                                       "all-gather of fp32 (O, LSE) + merge",
+                           "tokens_per_gpu": b - a, "algorithmic_bytes_per_step": alg,
+                           "attention_calls_per_s_one_layer": 1e3 / ms,
+                           "parallelism": f"sequence split x{world}",
+                           "execution": "CUDA graph replay of the whole step"},
+                "gpu_launches": args.steps * 2, "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["config2", "seqsplit128k"], default="config2",
+                    help="config2 (default, BASELINE configs[1]) or the 128k-token attention of "
+                         "configs[3] split across the GPUs (strong scaling)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-len", type=int, default=T,
                     help="tokens per sequence (profiling a smaller case only)")
@@ -347,7 +427,10 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=120),
                                              device_id=dev)
     try:
-        run_b200(args, rank, world, dev)
+        if args.workload == "seqsplit128k":
+            run_seqsplit(args, rank, world, dev)
+        else:
+            run_b200(args, rank, world, dev)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

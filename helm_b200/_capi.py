@@ -39,7 +39,7 @@ _SIGNATURES = {
         _P, _I, _I64,              # mask, mask_dtype, mask_stride_b
         _P, _I64, _I64, _P,        # out, strides, lse
         _P, _I64,                  # workspace, bytes
-        _I, _I, _I, _I, _I, _I,    # batch, hq, hkv, head_dim, page_size, dtype
+        _I, _I, _I, _I, _I, _I, _I,  # batch, hq, hkv, head_dim, page_size, dtype, out_dtype
         _F, _F, _I, _P]),          # scale, softcap, max_kv_len_hint, stream
     "helm_paged_decode_attention_noalloc": (_I, [
         _P, _I64, _I64, _P, _I64, _P, _I64, _I, _P, _P, _P, _P,
@@ -54,7 +54,7 @@ _SIGNATURES = {
         _I, _I, _I, _I, _I, _I, _P]),
     "helm_copy_pages": (_I, [_P, _P, _I64, _P, _P, _I64, _P]),
     "helm_gather_kv": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
-    "helm_merge_attention_states": (_I, [_P, _I, _P, _I, _I64, _I, _P, _I, _P, _P]),
+    "helm_merge_attention_states": (_I, [_P, _I, _I64, _P, _I64, _I, _I64, _I, _P, _I, _P, _P]),
 }
 
 _lib = None
@@ -214,6 +214,8 @@ def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torc
     dev = q.device
     if out is None:
         out = torch.empty(B, Hq, D, dtype=q.dtype, device=dev)
+    if out.dtype not in (q.dtype, torch.float32) or out.stride(2) != 1:
+        raise HelmError("out must be [B, Hq, D] in the query dtype or fp32, unit dim stride")
     ws_bytes = decode_workspace_bytes(dev, B, Hq, num_kv_heads, D)
     ws = _workspace(dev, ws_bytes, ((4 * B * num_kv_heads + 255) // 256) * 256)
     mask_ptr, mask_dt, mask_sb = None, 0, 0
@@ -231,7 +233,7 @@ def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torc
             mask_ptr, mask_dt, mask_sb,
             out.data_ptr(), out.stride(0), out.stride(1), _ptr(lse),
             ws.data_ptr(), ws.numel(),
-            B, Hq, num_kv_heads, D, page_size, helm_dtype(q.dtype),
+            B, Hq, num_kv_heads, D, page_size, helm_dtype(q.dtype), helm_dtype(out.dtype),
             float(scale), float(softcap or 0.0), int(max_kv_len_hint),
             _stream_handle(dev, stream))
     _check(rc, "helm_paged_decode_attention")
@@ -311,18 +313,22 @@ def gather_kv(pool: torch.Tensor, page_table: torch.Tensor, kv_lens: torch.Tenso
 
 def merge_attention_states(o_parts: torch.Tensor, lse_parts: torch.Tensor,
                            out_dtype: torch.dtype, stream=None):
-    """o_parts [R, ..., D], lse_parts fp32 [R, ...] -> (out [..., D], lse fp32 [...])."""
+    """o_parts [R, ..., D] (rows contiguous within a part, any part stride),
+    lse_parts fp32 [R, ...] -> (out [..., D] in out_dtype, lse fp32 [...])."""
     R = o_parts.shape[0]
     D = o_parts.shape[-1]
     rows = lse_parts[0].numel()
-    o_parts = o_parts.contiguous()
-    lse_parts = lse_parts.contiguous().float()
+    if o_parts[0].numel() != rows * D or not o_parts[0].is_contiguous():
+        raise HelmError("each part of o_parts must be a contiguous [rows, D] block")
+    if lse_parts.dtype != torch.float32 or not lse_parts[0].is_contiguous():
+        raise HelmError("lse_parts must be fp32 with contiguous parts")
     dev = o_parts.device
     out = torch.empty(o_parts.shape[1:], dtype=out_dtype, device=dev)
     lse = torch.empty(lse_parts.shape[1:], dtype=torch.float32, device=dev)
     with torch.cuda.device(dev):
         rc = lib().helm_merge_attention_states(
-            o_parts.data_ptr(), helm_dtype(o_parts.dtype), lse_parts.data_ptr(), R, rows, D,
+            o_parts.data_ptr(), helm_dtype(o_parts.dtype), o_parts.stride(0),
+            lse_parts.data_ptr(), lse_parts.stride(0), R, rows, D,
             out.data_ptr(), helm_dtype(out_dtype), lse.data_ptr(), _stream_handle(dev, stream))
     _check(rc, "helm_merge_attention_states")
     return out, lse

@@ -68,22 +68,25 @@ __device__ __forceinline__ void store_dt(void* p, int dt, int64_t i, float x) {
 }
 
 // One CTA per row (sequence, query head); threads stride over the head dim.
+// Part r's O row starts at o_parts + r*o_stride + row*D, its LSE at
+// lse_parts[r*lse_stride + row].
 __global__ void merge_states_kernel(const void* __restrict__ o_parts, int o_dtype,
-                                    const float* __restrict__ lse_parts, int parts, int64_t rows,
-                                    int head_dim, void* __restrict__ out, int out_dtype,
+                                    int64_t o_stride, const float* __restrict__ lse_parts,
+                                    int64_t lse_stride, int parts, int64_t rows, int head_dim,
+                                    void* __restrict__ out, int out_dtype,
                                     float* __restrict__ lse_out) {
   const int64_t row = blockIdx.x;
   float M = -INFINITY;
-  for (int r = 0; r < parts; ++r) M = fmaxf(M, lse_parts[r * rows + row]);
+  for (int r = 0; r < parts; ++r) M = fmaxf(M, lse_parts[r * lse_stride + row]);
   const float m_use = M == -INFINITY ? 0.f : M;
   float L = 0.f;
-  for (int r = 0; r < parts; ++r) L += expf(lse_parts[r * rows + row] - m_use);
+  for (int r = 0; r < parts; ++r) L += expf(lse_parts[r * lse_stride + row] - m_use);
   const float inv = L > 0.f ? 1.f / L : 0.f;
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float acc = 0.f;
     for (int r = 0; r < parts; ++r) {
-      const float w = expf(lse_parts[r * rows + row] - m_use);
-      if (w > 0.f) acc += w * load_dt(o_parts, o_dtype, (r * rows + row) * head_dim + d);
+      const float w = expf(lse_parts[r * lse_stride + row] - m_use);
+      if (w > 0.f) acc += w * load_dt(o_parts, o_dtype, r * o_stride + row * head_dim + d);
     }
     store_dt(out, out_dtype, row * head_dim + d, acc * inv);
   }
@@ -156,14 +159,15 @@ extern "C" int helm_gather_kv(const void* kv_pool, int64_t pool_pages, const int
   return HELM_OK;
 }
 
-extern "C" int helm_merge_attention_states(const void* o_parts, int o_dtype,
-                                           const float* lse_parts, int num_parts, int64_t rows,
-                                           int head_dim, void* out, int out_dtype, float* lse_out,
-                                           void* stream) {
+extern "C" int helm_merge_attention_states(const void* o_parts, int o_dtype, int64_t o_part_stride,
+                                           const float* lse_parts, int64_t lse_part_stride,
+                                           int num_parts, int64_t rows, int head_dim, void* out,
+                                           int out_dtype, float* lse_out, void* stream) {
   using namespace helm;
   if (o_parts == nullptr || lse_parts == nullptr || out == nullptr || num_parts <= 0 ||
       rows < 0 || head_dim <= 0)
     return HELM_ERR_INVALID_ARGUMENT;
+  if (o_part_stride < rows * head_dim || lse_part_stride < rows) return HELM_ERR_INVALID_ARGUMENT;
   auto dt_ok = [](int d) {
     return d == HELM_DTYPE_FP32 || d == HELM_DTYPE_BF16 || d == HELM_DTYPE_FP16;
   };
@@ -172,7 +176,8 @@ extern "C" int helm_merge_attention_states(const void* o_parts, int o_dtype,
   if (rows > 0x7fffffff) return HELM_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   merge_states_kernel<<<static_cast<unsigned>(rows), 128, 0, s>>>(
-      o_parts, o_dtype, lse_parts, num_parts, rows, head_dim, out, out_dtype, lse_out);
+      o_parts, o_dtype, o_part_stride, lse_parts, lse_part_stride, num_parts, rows, head_dim, out,
+      out_dtype, lse_out);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_last_cuda_error(e);

@@ -64,6 +64,7 @@ struct DecodeArgs {
   float* cta_ml;    // CTA partials [grid + pairs][G][2]
   int* counters;    // [B * Hkv] CTAs done per pair; zero between calls
   int batch, hq, hkv, group, page_size, tiles_per_page;
+  int out_fp32;  // O written as fp32 (partial states for a cross-device merge)
   float scale;
   float scale_log2;
   float softcap;
@@ -149,6 +150,17 @@ __device__ __forceinline__ float load_mask(const DecodeArgs& a, int b, int tok) 
   return __half2float(static_cast<const __half*>(a.mask)[off]);
 }
 
+// Writes one element of O (sequence b, query head qh, dim d).
+template <typename T>
+__device__ __forceinline__ void store_out(const DecodeArgs& a, int b, int qh, int d, float v) {
+  const int64_t off =
+      static_cast<int64_t>(b) * a.out_sb + static_cast<int64_t>(qh) * a.out_sh + d;
+  if (a.out_fp32)
+    static_cast<float*>(a.out)[off] = v;
+  else
+    static_cast<T*>(a.out)[off] = from_float<T>(v);
+}
+
 // Additive mask value in log2 units.  A finite mask (e.g. finfo(float32).min)
 // stays finite instead of overflowing to -inf, so a row whose every key is
 // masked with a finite value behaves as in eager fp32 arithmetic.
@@ -210,7 +222,6 @@ struct Worker {
     const int tb = s_cum[b + 1] - s_cum[b];
     const int st = s_cum[b] * a.hkv + h * tb;
     const bool alone = (st / W) == ((st + tb - 1) / W);
-    T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -220,11 +231,10 @@ struct Worker {
         if (hg >= a.group) continue;
         if (alone) {
           const float inv = 1.f / fmaxf(lt, 1e-12f);
-          T* oh = out + static_cast<int64_t>(h * a.group + hg) * a.out_sh;
 #pragma unroll
           for (int mt = 0; mt < KS; ++mt) {
-            oh[mt * 16 + g] = from_float<T>(o[nt][mt][j] * inv);
-            oh[mt * 16 + 8 + g] = from_float<T>(o[nt][mt][2 + j] * inv);
+            store_out<T>(a, b, h * a.group + hg, mt * 16 + g, o[nt][mt][j] * inv);
+            store_out<T>(a, b, h * a.group + hg, mt * 16 + 8 + g, o[nt][mt][2 + j] * inv);
           }
           if (g == 0 && a.lse != nullptr)
             a.lse[static_cast<int64_t>(b) * a.hq + h * a.group + hg] =
@@ -454,33 +464,71 @@ __device__ void merge_sources(const DecodeArgs& a, int p, const float* s_states,
     s_L[tid] = L;
   }
   consumer_barrier(kConsumers);
-  T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
-  for (int e = tid; e < G * D; e += kConsumers) {
-    const int hg = e / D, d = e - (e / D) * D;
-    float acc = 0.f;
-    for (int k0 = 0; k0 < K; k0 += kBatch) {
-      float o[kBatch];
+  // O: float4 elements (head, 4 dims); `groups` threads share an element and
+  // split its sources, each keeping kBatch loads in flight; partial sums meet
+  // in shared memory.
+  constexpr int D4 = D / 4;
+  const int E4 = G * D4;
+  const int groups = E4 >= kConsumers ? 1 : kConsumers / E4;
+  const int lanes = kConsumers / groups;  // threads per group
+  float4* s_red = reinterpret_cast<float4*>(
+      (reinterpret_cast<uintptr_t>(s_L + 16) + 15) & ~static_cast<uintptr_t>(15));
+  for (int e0 = 0; e0 < E4; e0 += lanes) {
+    const int grp = tid / lanes, e = e0 + (tid - grp * lanes);
+    const bool active = grp < groups && e < E4;
+    const int hg = active ? e / D4 : 0, d4 = active ? e - hg * D4 : 0;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (active) {
+      for (int k0 = grp * kBatch; k0 < K; k0 += groups * kBatch) {
+        float4 o[kBatch];
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i) {  // issue every load of the batch first
-        const int k = k0 + i;
-        o[i] = 0.f;
-        if (k < K) {
-          if (k < n_smem)
-            o[i] = s_states[(w0 + k) * kRec + 32 + hg * D + d];
-          else
-            o[i] = __ldcg(src_o(k) + hg * D + d);
+        for (int i = 0; i < kBatch; ++i) {  // issue the whole batch first
+          const int k = k0 + i;
+          o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (k < K) {
+            if (k < n_smem)
+              o[i] = *reinterpret_cast<const float4*>(s_states + (w0 + k) * kRec + 32 + hg * D +
+                                                     d4 * 4);
+            else
+              o[i] = __ldcg(reinterpret_cast<const float4*>(src_o(k) + hg * D + d4 * 4));
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kBatch; ++i) {
+          if (k0 + i < K) {
+            const float w = s_m[(k0 + i) * G + hg];
+            acc.x += w * o[i].x;
+            acc.y += w * o[i].y;
+            acc.z += w * o[i].z;
+            acc.w += w * o[i].w;
+          }
         }
       }
+    }
+    if (groups > 1) {
+      if (active) s_red[tid] = acc;
+      consumer_barrier(kConsumers);
+      if (active && grp == 0)
+        for (int q2 = 1; q2 < groups; ++q2) {
+          const float4 r = s_red[q2 * lanes + (tid - grp * lanes)];
+          acc.x += r.x;
+          acc.y += r.y;
+          acc.z += r.z;
+          acc.w += r.w;
+        }
+    }
+    if (active && grp == 0) {
+      const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+      if (final_out) {
+        const float inv = 1.f / fmaxf(s_L[hg], 1e-12f);
 #pragma unroll
-      for (int i = 0; i < kBatch; ++i)
-        if (k0 + i < K) acc += s_m[(k0 + i) * G + hg] * o[i];
+        for (int c = 0; c < 4; ++c) store_out<T>(a, b, h * G + hg, d4 * 4 + c, vals[c] * inv);
+      } else {
+        *reinterpret_cast<float4*>(a.cta_o + (static_cast<int64_t>(cta_out + p) * G + hg) * D +
+                                   d4 * 4) = acc;
+      }
     }
-    if (final_out) {
-      out[static_cast<int64_t>(h * G + hg) * a.out_sh + d] =
-          from_float<T>(acc / fmaxf(s_L[hg], 1e-12f));
-    } else {
-      a.cta_o[(static_cast<int64_t>(cta_out + p) * G + hg) * D + d] = acc;
-    }
+    if (groups > 1) consumer_barrier(kConsumers);
   }
   if (tid < G) {
     const float M = s_M[tid], L = s_L[tid];
@@ -566,9 +614,7 @@ __device__ void merge_global(const DecodeArgs& a, const MergeJob* jobs, int n_jo
       }
       const int p = jobs[j[i]].p;
       const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
-      T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
-      out[static_cast<int64_t>(h * G + hg[i]) * a.out_sh + d[i]] =
-          from_float<T>(acc / fmaxf(L, 1e-12f));
+      store_out<T>(a, b, h * G + hg[i], d[i], acc / fmaxf(L, 1e-12f));
       if (d[i] == 0 && a.lse != nullptr)
         a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg[i]] =
             (M == -INFINITY || L <= 0.f) ? -INFINITY : M * kLn2 + logf(L);
@@ -623,9 +669,8 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   for (int p = blockIdx.x; p < a.batch * a.hkv; p += gridDim.x) {
     const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
     if (s_cum[b + 1] != s_cum[b]) continue;
-    T* out = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.out_sb;
     for (int e = threadIdx.x; e < a.group * D; e += blockDim.x)
-      out[static_cast<int64_t>(h * a.group + e / D) * a.out_sh + e % D] = from_float<T>(0.f);
+      store_out<T>(a, b, h * a.group + e / D, e % D, 0.f);
     if (a.lse != nullptr && threadIdx.x < a.group)
       a.lse[static_cast<int64_t>(b) * a.hq + h * a.group + threadIdx.x] = -INFINITY;
   }
@@ -954,8 +999,8 @@ extern "C" int helm_paged_decode_attention(
     const int32_t* num_pages, const int32_t* page_used, const int32_t* page_start,
     const void* mask, int mask_dtype, int64_t mask_stride_b, void* out, int64_t out_stride_b,
     int64_t out_stride_h, float* lse, void* workspace, int64_t workspace_bytes, int batch,
-    int num_q_heads, int num_kv_heads, int head_dim, int page_size, int dtype, float scale,
-    float softcap, int max_kv_len_hint, void* stream) {
+    int num_q_heads, int num_kv_heads, int head_dim, int page_size, int dtype, int out_dtype,
+    float scale, float softcap, int max_kv_len_hint, void* stream) {
   using namespace helm;
   if (q == nullptr || kv_pool == nullptr || page_table == nullptr || kv_lens == nullptr ||
       out == nullptr || workspace == nullptr)
@@ -968,6 +1013,7 @@ extern "C" int helm_paged_decode_attention(
   if (group > 16) return HELM_ERR_UNSUPPORTED;
   if (batch > kMaxBatch) return HELM_ERR_UNSUPPORTED;
   if (dtype != HELM_DTYPE_BF16 && dtype != HELM_DTYPE_FP16) return HELM_ERR_UNSUPPORTED;
+  if (out_dtype != dtype && out_dtype != HELM_DTYPE_FP32) return HELM_ERR_UNSUPPORTED;
   if (head_dim != 64 && head_dim != 128 && head_dim != 256) return HELM_ERR_UNSUPPORTED;
   const bool ragged = num_pages != nullptr;
   if (ragged != (page_used != nullptr) || ragged != (page_start != nullptr))
@@ -1019,6 +1065,7 @@ extern "C" int helm_paged_decode_attention(
   a.group = group;
   a.page_size = page_size;
   a.tiles_per_page = (page_size + kTileRows - 1) / kTileRows;
+  a.out_fp32 = out_dtype == HELM_DTYPE_FP32 ? 1 : 0;
   a.scale = scale;
   a.scale_log2 = scale * kLog2e;
   a.softcap = softcap;

@@ -82,5 +82,5 @@ extern "C" int helm_paged_decode_attention_noalloc(
       q, q_stride_b, q_stride_h, kv_pool, pool_pages, page_table, pt_stride_b, max_pages, kv_lens,
       num_pages, page_used, page_start, mask, mask_dtype, mask_stride_b, out, out_stride_b,
       out_stride_h, lse, scratch, kNoAllocScratchBytes, batch, num_q_heads, num_kv_heads,
-      head_dim, page_size, dtype, scale, softcap, max_kv_len_hint, stream);
+      head_dim, page_size, dtype, dtype, scale, softcap, max_kv_len_hint, stream);
 }

@@ -90,7 +90,9 @@ int64_t helm_paged_decode_workspace_bytes(int batch, int num_q_heads, int num_kv
  *  mask         optional additive key mask [B, T] (row stride mask_stride_b),
  *               indexed by logical token position, dtype mask_dtype
  *  softcap      tanh soft-capping of the scaled scores when > 0
- *  out          [B, Hq, D] strides out_stride_b, out_stride_h
+ *  out          [B, Hq, D] strides out_stride_b, out_stride_h, in out_dtype: the
+ *               query dtype, or HELM_DTYPE_FP32 (partial states that another
+ *               device's results are merged with, see helm_merge_attention_states)
  *  lse          optional fp32 [B, Hq]
  *  workspace    >= helm_paged_decode_workspace_bytes(...) bytes, 256-byte aligned.
  *               Its first roundup(4*batch*num_kv_heads, 256) bytes are per-pair
@@ -109,12 +111,12 @@ int helm_paged_decode_attention(const void* q, int64_t q_stride_b, int64_t q_str
                                 void* out, int64_t out_stride_b, int64_t out_stride_h, float* lse,
                                 void* workspace, int64_t workspace_bytes, int batch,
                                 int num_q_heads, int num_kv_heads, int head_dim, int page_size,
-                                int dtype, float scale, float softcap, int max_kv_len_hint,
-                                void* stream);
+                                int dtype, int out_dtype, float scale, float softcap,
+                                int max_kv_len_hint, void* stream);
 
 /*
- * Same computation and arguments as helm_paged_decode_attention, without the
- * workspace: for callers that cannot allocate device memory, such as a server
+ * Same computation and arguments as helm_paged_decode_attention (output in the
+ * query dtype), without the workspace: for callers that cannot allocate device memory, such as a server
  * that gives all of HBM to its own pool at start-up (a later cudaMalloc would
  * fail or fragment it) or a decode loop that must not stall on the device-wide
  * synchronisation of cudaFree.  It has no counterpart in the reference (HELM
@@ -205,17 +207,20 @@ int helm_gather_kv(const void* kv_pool, int64_t pool_pages, const int32_t* page_
  * Merges R partial attention states over disjoint key ranges:
  *     M = max_r lse[r];  w_r = exp(lse[r] - M)
  *     out = sum_r w_r * o[r] / sum_r w_r,   lse_out = M + log(sum_r w_r)
- * o_parts [R, rows, D] (dtype o_dtype: fp32, bf16 or fp16), lse_parts fp32
- * [R, rows]; out [rows, D] in out_dtype; lse_out optional fp32 [rows].
- * rows = batch * num_q_heads.  A part with lse = -inf contributes nothing.
+ * Part r's O is [rows, D] at o_parts + r*o_part_stride elements (dtype o_dtype:
+ * fp32, bf16 or fp16) and its LSE [rows] at lse_parts + r*lse_part_stride
+ * (fp32), so one buffer gathered from R devices can be merged in place.  out
+ * [rows, D] in out_dtype; lse_out optional fp32 [rows].  rows = batch *
+ * num_q_heads.  A part with lse = -inf contributes nothing.
  *
  * No single-device counterpart in the reference (it is single-GPU); this is
  * the cross-rank form of its running-max rescale (helm/runtime/kv_cache.py:
  * 523-529) used by the sequence-split path.
  */
-int helm_merge_attention_states(const void* o_parts, int o_dtype, const float* lse_parts,
-                                int num_parts, int64_t rows, int head_dim, void* out,
-                                int out_dtype, float* lse_out, void* stream);
+int helm_merge_attention_states(const void* o_parts, int o_dtype, int64_t o_part_stride,
+                                const float* lse_parts, int64_t lse_part_stride, int num_parts,
+                                int64_t rows, int head_dim, void* out, int out_dtype,
+                                float* lse_out, void* stream);
 
 #ifdef __cplusplus
 }
