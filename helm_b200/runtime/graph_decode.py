@@ -1,0 +1,288 @@
+"""Decode steps replayed as CUDA graphs.
+
+The eager decode path (DecodeLoop + KVOffloadManager) launches ~15 kernels per
+layer from Python; at batch 1 that launch cost, not HBM, bounds the step.  Here
+one decode step of the whole model -- projections, fused append, paged
+attention, MLP, lm_head and the argmax that feeds the next step -- is captured
+once and replayed.  Everything that changes between steps lives in static
+device buffers refreshed by one host->device copy before each replay:
+
+  * the pool row of every layer's new K/V row (page bookkeeping, evictions and
+    their device->host copies run on the host first, in the reference's order);
+  * every layer's page table and length;
+  * the key mask row and the position counter.
+
+Cold (host-resident) pages are copied into per-layer staging slots INSIDE the
+graph on the copy stream: layer l's copy waits only for the attention of layer
+l-2 (the previous user of its staging half) and runs while layers l-1 and l
+compute; attention(l) waits for it.  The copy nodes have fixed addresses, so
+the graph is captured again whenever the set of cold pages changes (when pages
+are evicted: once per page-fill period at most).  Pools are sized up front so
+that no captured pointer moves.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .. import _capi
+from .kv_cache import _stager_for
+
+
+class _GraphContext:
+    """Static device state read by the patched attention forwards."""
+
+    def __init__(self, mgr, B: int, Hq: int, D: int, L: int, max_len: int, dtype, dev):
+        self.mgr = mgr
+        self.B, self.Hq, self.D, self.L = B, Hq, D, L
+        self.max_len = max_len
+        self.P = mgr.config.page_size
+        self.maxp = -(-max_len // self.P)
+        self.dev = dev
+        self.pool = mgr.allocator.pool_for(dev)
+        self.q_out = torch.empty(L, B, Hq, D, dtype=dtype, device=dev)
+        self.attn_out = torch.empty(L, B, Hq, D, dtype=dtype, device=dev)
+        # blob: rows int64 [L, B] | lens int32 [L, B] | tables int32 [L, B, maxp]
+        n32 = L * B + L * B * self.maxp
+        self.blob_bytes = L * B * 8 + n32 * 4
+        self.blob = torch.zeros(self.blob_bytes, dtype=torch.uint8, device=dev)
+        self.rows = self.blob[:L * B * 8].view(torch.int64).view(L, B)
+        rest = self.blob[L * B * 8:].view(torch.int32)
+        self.lens = rest[:L * B].view(L, B)
+        self.tables = rest[L * B:].view(L, B, self.maxp)
+        self.host = [torch.zeros(self.blob_bytes, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.host_ev = [None, None]
+        self.flip = 0
+        self.mask2d = torch.zeros(B, max_len, dtype=dtype, device=dev)
+        self.mask4d = self.mask2d.view(B, 1, 1, max_len)
+        # cold pages: per layer [(host pool, host slots, staging slots)]
+        self.cold_plan: list = [[] for _ in range(L)]
+        self.copy_stream = torch.cuda.Stream(dev)
+        self.copy_done = [torch.cuda.Event() for _ in range(L)]
+        self.attn_done = [torch.cuda.Event() for _ in range(L)]
+        self.capturing = False
+
+    # -- copies of cold pages inside the captured step --------------------------
+    def _issue_copies(self, l: int) -> None:
+        for host_pool, srcs, dsts in self.cold_plan[l]:
+            _capi.copy_pages(self.pool.storage, host_pool.storage, dsts, srcs, self.dev,
+                             stream=self.copy_stream)
+        self.copy_done[l].record(self.copy_stream)
+
+    def begin_step(self) -> None:
+        cur = torch.cuda.current_stream(self.dev)
+        self.copy_stream.wait_stream(cur)
+        for l in (0, 1):
+            if l < self.L and self.cold_plan[l]:
+                with torch.cuda.stream(self.copy_stream):
+                    self._issue_copies(l)
+
+    def before_attention(self, l: int) -> None:
+        if self.cold_plan[l]:
+            torch.cuda.current_stream(self.dev).wait_event(self.copy_done[l])
+
+    def after_attention(self, l: int) -> None:
+        nxt = l + 2
+        if nxt < self.L and self.cold_plan[nxt]:
+            self.attn_done[l].record(torch.cuda.current_stream(self.dev))
+            self.copy_stream.wait_event(self.attn_done[l])
+            with torch.cuda.stream(self.copy_stream):
+                self._issue_copies(nxt)
+
+    def end_step(self) -> None:
+        torch.cuda.current_stream(self.dev).wait_stream(self.copy_stream)
+
+
+def graph_attention_forward(attn_self, kvcms, ctx: _GraphContext, hidden_states,
+                            position_embeddings, q_norm=None, k_norm=None):
+    """Decode forward of one attention module inside a captured step."""
+    l = attn_self.layer_idx
+    B = hidden_states.shape[0]
+    D = attn_self.head_dim
+    q = attn_self.q_proj(hidden_states).view(B, -1, D)
+    k = attn_self.k_proj(hidden_states).view(B, -1, D)
+    v = attn_self.v_proj(hidden_states).view(B, -1, D)
+    cos, sin = position_embeddings
+    _capi.kv_append(q=q, k=k, v=v, q_out=ctx.q_out[l],
+                    q_norm_w=None if q_norm is None else q_norm.weight,
+                    k_norm_w=None if k_norm is None else k_norm.weight,
+                    eps=1e-6 if q_norm is None else q_norm.variance_epsilon,
+                    cos=cos.reshape(B, D), sin=sin.reshape(B, D), pool=ctx.pool.storage,
+                    slot_rows=ctx.rows[l], page_size=ctx.P)
+    ctx.before_attention(l)
+    _capi.paged_decode_attention(ctx.q_out[l], ctx.pool.storage, ctx.tables[l], ctx.lens[l],
+                                 num_kv_heads=k.shape[1], page_size=ctx.P,
+                                 scale=1.0 / math.sqrt(D), mask=None,
+                                 out=ctx.attn_out[l], max_kv_len_hint=ctx.max_len)
+    ctx.after_attention(l)
+    return attn_self.o_proj(ctx.attn_out[l].view(B, 1, -1)), None
+
+
+class GraphDecoder:
+    """Greedy generation with graph-replayed decode steps (batch of equal-length
+    prompts, dense page lists).  Produces the same tokens as DecodeLoop."""
+
+    def __init__(self, model, kv_offload_mgr, max_len: int):
+        self.model = model
+        self.mgr = kv_offload_mgr
+        self.max_len = max_len
+        cfg = model.config
+        self.L = cfg.num_hidden_layers
+        self.D = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        self.Hq = cfg.num_attention_heads
+        self.dtype = next(model.parameters()).dtype
+        self.dev = next(model.parameters()).device
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.ctx: Optional[_GraphContext] = None
+        self.cold_sig = None
+        self.captures = 0
+
+    # -- host side of a step ------------------------------------------------------
+    def _plan(self) -> None:
+        """Bookkeeping of one decode token on every layer (reference order), then
+        the per-layer rows, lengths and page tables into the pinned blob."""
+        from .kv_offload import _finish_rows, _reserve_rows
+        ctx, kvcms = self.ctx, self.mgr.kvcms
+        rows = np.empty((self.L, ctx.B), np.int64)
+        try:
+            for l in range(self.L):
+                rows[l] = _reserve_rows(kvcms, l, self.dev)
+        finally:
+            _finish_rows(kvcms, self.dev)   # eviction copies queue before the replay
+        lens = np.zeros((self.L, ctx.B), np.int32)
+        tables = np.zeros((self.L, ctx.B, ctx.maxp), np.int32)
+        cold_sig = []
+        stager = _stager_for(ctx.pool)
+        plans = []
+        for l in range(self.L):
+            plan, n_staged, sig = {}, 0, []
+            for b, kvcm in enumerate(kvcms):
+                layer = kvcm.layers[l]
+                if layer._ragged or not layer._table_ok():
+                    raise NotImplementedError("graph decode needs dense page lists "
+                                              "(prefill chunks that are a multiple of the page size)")
+                n = layer._n
+                if n > ctx.maxp:
+                    raise ValueError("sequence longer than the graph's max_len")
+                lens[l, b] = layer.total_tokens
+                slots = layer._slots[:n].copy()
+                if layer._cold:
+                    for i in np.nonzero(slots < 0)[0]:
+                        page = layer.pages[i]
+                        s = stager._slot(l & 1, n_staged)
+                        n_staged += 1
+                        slots[i] = s
+                        plan.setdefault(id(page.pool), (page.pool, [], []))
+                        plan[id(page.pool)][1].append(page.slot)
+                        plan[id(page.pool)][2].append(s)
+                        sig.append((page.page_id, page.generation))
+                tables[l, b, :n] = slots
+            plans.append(list(plan.values()))
+            cold_sig.append(tuple(sig))
+        ctx.cold_plan = plans
+        h = ctx.host[ctx.flip]
+        if ctx.host_ev[ctx.flip] is not None:
+            ctx.host_ev[ctx.flip].synchronize()
+        hv = h.numpy()
+        o = 0
+        hv[o:o + rows.nbytes] = rows.view(np.uint8).reshape(-1)
+        o += rows.nbytes
+        hv[o:o + lens.nbytes] = lens.view(np.uint8).reshape(-1)
+        o += lens.nbytes
+        hv[o:o + tables.nbytes] = tables.view(np.uint8).reshape(-1)
+        ctx.blob.copy_(h, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.dev))
+        ctx.host_ev[ctx.flip] = ev
+        ctx.flip ^= 1
+        ptrs = tuple(p.storage.data_ptr() for p in self.mgr.allocator.pools()
+                     if p.storage is not None)
+        self._pending_sig = (tuple(cold_sig), ptrs)
+
+    def _step_body(self) -> None:
+        ctx = self.ctx
+        ctx.begin_step()
+        out = self.model(input_ids=self.ids, attention_mask=ctx.mask4d, position_ids=self.pos,
+                         use_cache=False, logits_to_keep=1)
+        self.logits.copy_(out.logits[:, -1, :])
+        self.ids.copy_(torch.argmax(self.logits, dim=-1, keepdim=True))
+        self.pos.add_(1)
+        ctx.end_step()
+
+    def _capture(self) -> None:
+        self.graph = None
+        torch.cuda.synchronize(self.dev)
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        saved = (self.ids.clone(), self.pos.clone())
+        self.mgr.kvcms[0]._graph = self.ctx
+        try:
+            with torch.cuda.graph(g, stream=side):
+                self._step_body()
+        finally:
+            self.mgr.kvcms[0]._graph = None
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        torch.cuda.synchronize(self.dev)
+        # capture does not execute: state is unchanged, but be explicit
+        self.ids.copy_(saved[0])
+        self.pos.copy_(saved[1])
+        self.graph = g
+        self.captures += 1
+        self.cold_sig = self._pending_sig
+
+    @torch.no_grad()
+    def generate(self, input_ids, max_new_tokens: int, keep_logits: bool = False,
+                 reserve_pages: bool = True):
+        from .decode_loop import DecodeLoop
+        B, S = input_ids.shape
+        if S + max_new_tokens > self.max_len:
+            raise ValueError("prompt + new tokens exceed max_len")
+        loop = DecodeLoop(self.model, self.mgr)
+        self.mgr.reset()
+        pool = self.mgr.allocator.pool_for(self.dev)
+        if reserve_pages:  # pointers captured in the graph must never move
+            pages = self.L * B * (-(-self.max_len // self.mgr.config.page_size))
+            if pool.capacity - pool.next_slot < 2 * pages + 16:
+                pool.reserve_capacity(2 * pages + 16)
+            host = self.mgr.allocator.pool_for(torch.device("cpu"))
+            if host.capacity - host.next_slot < pages + 16:
+                host.reserve_capacity(pages + 16)
+        logits0 = loop.prefill(input_ids)
+        self.ctx = _GraphContext(self.mgr, B, self.Hq, self.D, self.L, self.max_len, self.dtype,
+                                 self.dev)
+        self.ids = torch.argmax(logits0, dim=-1, keepdim=True)
+        self.pos = torch.full((B, 1), S, dtype=torch.long, device=self.dev)
+        self.logits = torch.empty_like(logits0)
+        history = torch.empty(B, max_new_tokens, dtype=torch.long, device=self.dev)
+        history[:, 0] = self.ids[:, 0]
+        all_logits = [logits0.float()] if keep_logits else None
+        # one eager step primes workspaces and attributes before any capture
+        for step in range(1, max_new_tokens):
+            self._plan()
+            if self.graph is None or self._pending_sig != self.cold_sig:
+                if step == 1:
+                    self._eager_step()
+                    history[:, step] = self.ids[:, 0]
+                    if keep_logits:
+                        all_logits.append(self.logits.float().clone())
+                    continue
+                self._capture()
+            self.graph.replay()
+            history[:, step] = self.ids[:, 0]
+            if keep_logits:
+                all_logits.append(self.logits.float().clone())
+        out = (history, all_logits) if keep_logits else history
+        self.graph = None   # captured pointers belong to this request
+        return out
+
+    def _eager_step(self) -> None:
+        """The captured body run once without capture (same bookkeeping)."""
+        self.mgr.kvcms[0]._graph = self.ctx
+        try:
+            self._step_body()
+        finally:
+            self.mgr.kvcms[0]._graph = None

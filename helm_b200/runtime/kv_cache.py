@@ -23,6 +23,7 @@ implementation.  K/V dtypes are bf16 and fp16; head_dim 64, 128 or 256.
 """
 from __future__ import annotations
 
+import heapq
 import math
 import os
 from dataclasses import dataclass, field
@@ -530,6 +531,16 @@ class KVCacheManager:
         self.gpu_high_watermark_bytes = gpu_high_watermark_bytes
         self.sync_evictions = sync_evictions
         self._evicted = False
+        # Residency bookkeeping kept in step with every append and eviction so
+        # that the watermark check is O(1) and eviction O(log n), instead of
+        # the reference's scan of every page of every layer per append.  Same
+        # decisions: a heap of the evictable pages (GPU, full, not a tail)
+        # keyed (start_token, layer order, page index) is the reference's
+        # stable sort by start_token over layers in dict order.
+        self._heap: list = []
+        self._n_evictable = 0
+        self._rank_counter = 0
+        self._fingerprint: tuple = ()
         self.cont_K: dict = {}
         self.cont_V: dict = {}
         self.cont_capacity: int = 0
@@ -540,12 +551,62 @@ class KVCacheManager:
 
     def initialize_layer_caches(self, num_layers: int):
         for i in range(num_layers):
-            self.layers[i] = LayerKVCache(layer_id=i)
+            self._insert_layer(i)
+
+    def _insert_layer(self, layer_id: int) -> LayerKVCache:
+        layer = LayerKVCache(layer_id)
+        layer._rank = self._rank_counter
+        self._rank_counter += 1
+        self.layers[layer_id] = layer
+        self._fingerprint = tuple(map(id, self.layers.values()))
+        return layer
 
     def _layer(self, layer_id: int) -> LayerKVCache:
         if layer_id not in self.layers:
-            self.layers[layer_id] = LayerKVCache(layer_id)
+            return self._insert_layer(layer_id)
         return self.layers[layer_id]
+
+    # -- incremental residency tracking -------------------------------------------
+    @staticmethod
+    def _is_evictable(layer: LayerKVCache, page: KVPage) -> bool:
+        return page.state == "GPU" and page.device.type == "cuda" and page is not layer.tail_page \
+            and page.used_tokens == page.capacity_tokens
+
+    def _tracking_ok(self) -> bool:
+        if self._fingerprint != tuple(map(id, self.layers.values())):
+            return False
+        return all(hasattr(L, "_rank") and L._table_ok() for L in self.layers.values())
+
+    def _retrack(self) -> None:
+        """Rebuilds the evictable heap from a scan (after direct edits)."""
+        for layer in self.layers.values():
+            if not hasattr(layer, "_rank"):
+                layer._rank = self._rank_counter
+                self._rank_counter += 1
+            if not layer._table_ok():
+                _rebuild_table(layer)
+        # ranks must follow the dict order of self.layers
+        order = sorted(self.layers.values(), key=lambda L: L._rank)
+        if [id(L) for L in order] != [id(L) for L in self.layers.values()]:
+            for L in self.layers.values():
+                L._rank = self._rank_counter
+                self._rank_counter += 1
+        self._heap = []
+        for layer in self.layers.values():
+            for idx, page in enumerate(layer.pages):
+                if self._is_evictable(layer, page):
+                    self._heap.append((page.start_token, layer._rank, idx, id(page), layer, page))
+        heapq.heapify(self._heap)
+        self._n_evictable = len(self._heap)
+        self._fingerprint = tuple(map(id, self.layers.values()))
+
+    def _note_new_tail(self, layer: LayerKVCache, old_tail: Optional[KVPage]) -> None:
+        """A page was appended: the previous tail may have become evictable."""
+        if old_tail is not None and self._is_evictable(layer, old_tail):
+            idx = len(layer.pages) - 2
+            heapq.heappush(self._heap, (old_tail.start_token, layer._rank, idx, id(old_tail),
+                                        layer, old_tail))
+            self._n_evictable += 1
 
     # -- appends: bookkeeping in the reference's order, data in one transfer --
     def _new_page(self, layer: LayerKVCache, layer_id: int, device, used: int) -> KVPage:
@@ -555,8 +616,11 @@ class KVCacheManager:
         page.used_tokens = used
         if not layer._table_ok():
             _rebuild_table(layer)
+        old_tail = layer.tail_page
         layer.append_page(page)
         layer._track_new(page)
+        if hasattr(layer, "_rank"):
+            self._note_new_tail(layer, old_tail)
         return page
 
     def _begin(self):
@@ -665,27 +729,28 @@ class KVCacheManager:
         """Global oldest-page-first eviction to the host tier (kv_cache.py:179-222)."""
         if bytes_to_evict <= 0:
             return
-        gpu_pages = self._evictable()
-        gpu_pages.sort(key=lambda t: t[1].start_token)
+        if not self._tracking_ok():
+            self._retrack()
         evicted_bytes = 0
         n_moved = 0
         direct = self.allocator._deferred is None
         dev = None
-        for layer, page in gpu_pages:
-            if evicted_bytes >= bytes_to_evict:
-                break
+        while self._heap and evicted_bytes < bytes_to_evict:
+            _, _, idx, _, layer, page = heapq.heappop(self._heap)
+            if not (idx < len(layer.pages) and layer.pages[idx] is page
+                    and self.layers.get(layer.layer_id) is layer
+                    and self._is_evictable(layer, page)):
+                continue  # stale entry
+            self._n_evictable -= 1
             original_start = page.start_token
             dev = page.device
-            table_ok = layer._table_ok()
             new_page = self.allocator.move_page(page, torch.device("cpu"))
             assert new_page.start_token == original_start, "Page invariant broken during migration"
-            idx = next(i for i, p in enumerate(layer.pages) if p is page)
             layer.pages[idx] = new_page
             if layer.tail_page is page:
                 layer.tail_page = new_page
-            if table_ok:
-                layer._slots[idx] = _slot_code(new_page)
-                layer._cold += 1
+            layer._slots[idx] = _slot_code(new_page)
+            layer._cold += 1
             evicted_bytes += new_page.k_tensor.numel() * new_page.k_tensor.element_size() * 2
             n_moved += 1
         if n_moved:
@@ -695,8 +760,15 @@ class KVCacheManager:
                 self._evicted = False
         _record_eviction(n_moved, evicted_bytes)
 
+    def _evictable_count(self) -> int:
+        if not self._tracking_ok():
+            self._retrack()
+        if os.environ.get("HELM_B200_CHECK_RESIDENCY"):
+            assert self._n_evictable == len(self._evictable()), "residency tracking diverged"
+        return self._n_evictable
+
     def _enforce_residency_policy(self):
-        gpu_bytes = self.allocator.bytes_per_page * len(self._evictable())
+        gpu_bytes = self.allocator.bytes_per_page * self._evictable_count()
         if gpu_bytes > self.gpu_high_watermark_bytes:
             self.evict_pages(gpu_bytes - self.gpu_high_watermark_bytes)
 
@@ -719,6 +791,9 @@ class KVCacheManager:
             layer.total_tokens = 0
             _rebuild_table(layer)
         self.layers.clear()
+        self._heap = []
+        self._n_evictable = 0
+        self._fingerprint = ()
 
     def all_gpu_resident(self, layer_id: int) -> bool:
         if layer_id not in self.layers:

@@ -269,6 +269,11 @@ def _make_forward(kvcms, *, qk_norm: bool = False, norm_whole: bool = False,
         scale = getattr(attn_self, "scaling", 1.0 / math.sqrt(attn_self.head_dim)) if gemma2 \
             else 1.0 / math.sqrt(attn_self.head_dim)
         softcap = getattr(attn_self, "attn_logit_softcapping", None) if gemma2 else None
+        ctx = getattr(kvcms[0], "_graph", None)
+        if ctx is not None and q_len == 1 and not norm_whole and not gemma2:
+            from .graph_decode import graph_attention_forward
+            return graph_attention_forward(attn_self, kvcms, ctx, hidden_states,
+                                           position_embeddings, qn, kn)
         if q_len == 1 and not norm_whole:
             mask = attention_mask
             if gemma2:

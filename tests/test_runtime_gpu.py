@@ -41,7 +41,10 @@ def _close(got, ref, dtype):
 
 
 # ── placement ──────────────────────────────────────────────────────────────────
-def test_gpu_tier_placement_matches_reference(dev, placement_golden):
+def test_gpu_tier_placement_matches_reference(dev, placement_golden, monkeypatch):
+    # also assert, at every residency decision, that the incremental evictable
+    # count equals a full scan of the pages
+    monkeypatch.setenv("HELM_B200_CHECK_RESIDENCY", "1")
     n = 0
     for entry in placement_golden:
         sc = entry["scenario"]
