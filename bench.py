@@ -398,21 +398,149 @@ def run_seqsplit(args, rank: int, world: int, dev: torch.device):
         print(json.dumps(line), flush=True)
 
 
+MODEL_WORKLOADS = {
+    # Qwen3-0.6B, 512-token prompt, 64 greedy steps, 64-token pages,
+    # kv-offload on at the reference's default watermark (no page is evicted at 576 tokens)
+    "config1": dict(arch="qwen3-0.6b", batch=1, prompt=512, steps=64, page=64, cold=0.0),
+    # Qwen3-8B, 4096-token prompt, 256 steps, the oldest 75% of the
+    # prompt's pages held in pinned host memory and staged per layer inside the step
+    "config3": dict(arch="qwen3-8b", batch=1, prompt=4096, steps=256, page=64, cold=0.75),
+}
+
+
+def _h2d_gbs(dev: torch.device, nbytes: int = 1 << 30) -> float:
+    """Pinned host -> device copy bandwidth (best of 5), the link roofline."""
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    best = 0.0
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        d.copy_(h, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        best = max(best, nbytes / (e0.elapsed_time(e1) / 1e3) / 1e9)
+    del h, d
+    return best
+
+
+def run_model(args, rank: int, world: int, dev: torch.device):
+    """Decode tok/s of a whole model: random-init
+    weights, random prompt, greedy decode through KVOffloadManager + GraphDecoder
+    (every decode step one CUDA graph replay).  Timed: exactly K decode steps
+    (steps 1..K of one generate call) with CUDA events, host bookkeeping and
+    any re-capture included.  Every rank runs its own replica (weak scaling)."""
+    from helm_b200.runtime.graph_decode import GraphDecoder
+    from helm_b200.runtime.kv_cache import get_paging_stats, reset_paging_stats
+    from helm_b200.runtime.kv_offload import KVOffloadConfig, KVOffloadManager
+    from helm_b200.synthetic import build_model, make_config
+    from helm_b200 import _capi
+    w = MODEL_WORKLOADS[args.workload]
+    K = args.steps if args.steps_given else w["steps"]
+    cfg = make_config(w["arch"])
+    model = build_model(cfg, seed=0, std=0.02, dtype=torch.bfloat16, device=dev)
+    model.eval()
+    Bq, S = w["batch"], w["prompt"]
+    prompt = torch.randint(0, cfg.vocab_size, (Bq, S), generator=torch.Generator().manual_seed(0))
+    prompt = prompt.pin_memory()
+    L, Hkv, Dh = cfg.num_hidden_layers, cfg.num_key_value_heads, cfg.head_dim
+    tok_bytes = 2 * Hkv * Dh * 2                       # K+V of one token of one layer
+    wm = None
+    if w["cold"] > 0:     # keep the newest (1 - cold) of the prompt's pages on the GPU
+        wm = int((1 - w["cold"]) * S * tok_bytes * L)
+    kcfg = KVOffloadConfig.from_model(model, page_size=w["page"], gpu_watermark_bytes=wm)
+    mgr = KVOffloadManager(model, kcfg)
+    gd = GraphDecoder(model, mgr, max_len=S + K + 1)
+    try:
+        for _ in range(max(args.warmup, 3)):
+            gd.generate(prompt.to(dev, non_blocking=True), 4)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        reset_paging_stats()
+        with ClockSampler(dev.index) as clocks:
+            t0 = time.perf_counter()
+            toks = gd.generate(prompt.to(dev, non_blocking=True), K + 1)
+            toks_host = toks.cpu()
+            wall = time.perf_counter() - t0
+        ms = gd.decode_ms() / K
+        stats = get_paging_stats()
+        h2d_step = gd.h2d_bytes / K
+        plan_ms = gd.plan_seconds * 1e3 / K
+        captures = gd.captures
+    finally:
+        mgr.restore()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    if _capi.device_status(dev) != 0:
+        raise RuntimeError("device status reported an error")
+    if rank != 0:
+        return
+    n_params = sum(p.numel() for p in model.parameters())
+    embed = model.get_input_embeddings().weight
+    tied = model.get_output_embeddings().weight.data_ptr() == embed.data_ptr()
+    # every weight is read once per step; an untied input embedding only by its B rows
+    weight_bytes = (n_params - (0 if tied else embed.numel())) * 2
+    mean_ctx = S + (K + 1) / 2
+    kv_step = L * Bq * mean_ctx * tok_bytes
+    step_bytes = weight_bytes + kv_step
+    hbm, peak_src = _peaks()
+    link = _h2d_gbs(dev)
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    t_floor = max(step_bytes / (hbm * 1e9), h2d_step / (link * 1e9)) * 1e3
+    line = {"metric": METRIC, "value": world * Bq / (ms / 1e3), "unit": "tok/s",
+            "n_gpus": world, "steps": K, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random-init weights, uniform random prompt)",
+            "config": {"workload": f"{args.workload}: {w['arch']} random-init bf16, batch {Bq}, "
+                                   f"{S}-token prompt, {K} greedy decode steps, "
+                                   f"{w['page']}-token pages, "
+                                   f"{int(w['cold'] * 100)}% of prompt pages host-resident",
+                       "execution": "one CUDA graph replay per decode step (re-captured when "
+                                    "the cold page set changes)",
+                       "l2": "weights + KV per step exceed L2",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "bytes_per_step": step_bytes, "weight_bytes": weight_bytes,
+                         "kv_bytes_per_step_mean": kv_step,
+                         "h2d_bytes_per_step": h2d_step, "h2d_link_gbs_measured": link,
+                         "step_floor_ms": t_floor, "frac_of_floor": t_floor / ms,
+                         "peak_source": peak_src},
+            "e2e": {"value": Bq * (K + 1) / wall, "unit": "tok/s",
+                    "h2d_bytes_per_step": prompt.numel() * 8 / (K + 1),
+                    "d2h_bytes_per_step": toks_host.numel() * 8 / (K + 1),
+                    "note": "one generate() call from a pinned host prompt to host tokens, "
+                            "prefill and graph captures included"},
+            "host_plan_ms_per_step": plan_ms, "graph_captures": captures,
+            "paging": stats,
+            # this library's kernels per step: fused append + paged attention per layer
+            "gpu_launches": 2 * L * K, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["config2", "seqsplit128k"], default="config2",
-                    help="config2 (default, BASELINE configs[1]) or the 128k-token attention of "
-                         "configs[3] split across the GPUs (strong scaling)")
+    ap.add_argument("--workload", choices=["config2", "seqsplit128k"] + sorted(MODEL_WORKLOADS),
+                    default="config2",
+                    help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
+                         "configs[3] split across the GPUs (strong scaling); or whole-model "
+                         "decode tok/s of configs[0] (config1) / configs[2] (config3)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-len", type=int, default=T,
                     help="tokens per sequence (profiling a smaller case only)")
     ap.add_argument("--pool-pages", type=int, default=POOL,
                     help="page-pool slots (profiling a smaller case only)")
     args = ap.parse_args()
+    args.steps_given = args.steps is not None
+    if args.steps is None:
+        args.steps = 50
     _set_shape(args.seq_len, args.pool_pages)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -429,6 +557,8 @@ def main():
     try:
         if args.workload == "seqsplit128k":
             run_seqsplit(args, rank, world, dev)
+        elif args.workload in MODEL_WORKLOADS:
+            run_model(args, rank, world, dev)
         else:
             run_b200(args, rank, world, dev)
     finally:

@@ -23,13 +23,53 @@ that no captured pointer moves.
 from __future__ import annotations
 
 import math
+import time
 from typing import Optional
 
 import numpy as np
 import torch
 
 from .. import _capi
-from .kv_cache import _stager_for
+from .kv_allocator import ARENA_SLOTS
+from .kv_cache import _page_bytes_used, _record_prefetch, _stager_for
+
+
+class _ColdPages:
+    """A layer's host-resident pages as the step plan needs them; rebuilt only
+    when the layer's cold set changes (an eviction or a re-derived table)."""
+    __slots__ = ("key", "idx", "host_slots", "groups", "sig", "used_bytes")
+
+
+def _cold_pages(layer) -> _ColdPages:
+    key = (layer._cold, layer._epoch, layer._n)
+    cc = getattr(layer, "_graph_cold", None)
+    if cc is not None and cc.key[:2] == key[:2] and cc.key[2] <= key[2]:
+        return cc   # only hot pages were appended since
+    cc = _ColdPages()
+    cc.key = key
+    cc.idx = np.nonzero(layer._slots[:layer._n] < 0)[0]
+    pages = [layer.pages[i] for i in cc.idx]
+    cc.host_slots = np.array([p.slot for p in pages], np.int64)
+    pools: dict = {}
+    for j, p in enumerate(pages):
+        pools.setdefault(id(p.pool), (p.pool, []))[1].append(j)
+    cc.groups = [(pool, np.array(sel, np.intp)) for pool, sel in pools.values()]
+    cc.sig = tuple((p.page_id, p.generation) for p in pages)
+    cc.used_bytes = sum(_page_bytes_used(p) for p in pages)
+    layer._graph_cold = cc
+    return cc
+
+
+def _stage_slots(stager, parity: int, a: int, b: int) -> np.ndarray:
+    """Staging slots [a, b) of one half as an array (the half grows on demand)."""
+    if b > a:
+        stager._slot(parity, b - 1)
+    half = stager.halves[parity]
+    cache = stager.__dict__.setdefault("_graph_np", [None, None])
+    arr = cache[parity]
+    if arr is None or len(arr) != len(half):
+        arr = cache[parity] = np.asarray(half, np.int64)
+    return arr[a:b]
 
 
 class _GraphContext:
@@ -54,6 +94,13 @@ class _GraphContext:
         self.lens = rest[:L * B].view(L, B)
         self.tables = rest[L * B:].view(L, B, self.maxp)
         self.host = [torch.zeros(self.blob_bytes, dtype=torch.uint8).pin_memory() for _ in range(2)]
+        self.host_views = []
+        for h in self.host:
+            hv = h.numpy()
+            r = hv[:L * B * 8].view(np.int64).reshape(L, B)
+            rest = hv[L * B * 8:].view(np.int32)
+            self.host_views.append((r, rest[:L * B].reshape(L, B),
+                                    rest[L * B:].reshape(L, B, self.maxp)))
         self.host_ev = [None, None]
         self.flip = 0
         self.mask2d = torch.zeros(B, max_len, dtype=dtype, device=dev)
@@ -139,26 +186,35 @@ class GraphDecoder:
         self.ctx: Optional[_GraphContext] = None
         self.cold_sig = None
         self.captures = 0
+        self.h2d_bytes = 0
 
     # -- host side of a step ------------------------------------------------------
     def _plan(self) -> None:
         """Bookkeeping of one decode token on every layer (reference order), then
-        the per-layer rows, lengths and page tables into the pinned blob."""
-        from .kv_offload import _finish_rows, _reserve_rows
-        ctx, kvcms = self.ctx, self.mgr.kvcms
-        rows = np.empty((self.L, ctx.B), np.int64)
+        the per-layer rows, lengths and page tables, written straight into the
+        pinned upload buffer of this step."""
+        from .kv_offload import _finish_rows
+        ctx, kvcms, P = self.ctx, self.mgr.kvcms, self.ctx.P
+        if ctx.host_ev[ctx.flip] is not None:   # the buffer's previous upload is done
+            ctx.host_ev[ctx.flip].synchronize()
+        rows, lens, tables = ctx.host_views[ctx.flip]
+        for kvcm in kvcms:
+            kvcm._begin()
+            if not kvcm._tracking_ok():
+                kvcm._retrack()
         try:
             for l in range(self.L):
-                rows[l] = _reserve_rows(kvcms, l, self.dev)
+                for b, kvcm in enumerate(kvcms):
+                    _, _, slot, _, _, r0 = kvcm._reserve_decode_row(l, self.dev)
+                    rows[l, b] = slot * P + r0
+                    kvcm._enforce_residency_tracked()
         finally:
             _finish_rows(kvcms, self.dev)   # eviction copies queue before the replay
-        lens = np.zeros((self.L, ctx.B), np.int32)
-        tables = np.zeros((self.L, ctx.B, ctx.maxp), np.int32)
-        cold_sig = []
         stager = _stager_for(ctx.pool)
-        plans = []
+        plans, cold_sig = [], []
         for l in range(self.L):
-            plan, n_staged, sig = {}, 0, []
+            parity, n_staged, sig, groups = l & 1, 0, [], {}
+            n_cold, cold_bytes = 0, 0
             for b, kvcm in enumerate(kvcms):
                 layer = kvcm.layers[l]
                 if layer._ragged or not layer._table_ok():
@@ -168,32 +224,29 @@ class GraphDecoder:
                 if n > ctx.maxp:
                     raise ValueError("sequence longer than the graph's max_len")
                 lens[l, b] = layer.total_tokens
-                slots = layer._slots[:n].copy()
-                if layer._cold:
-                    for i in np.nonzero(slots < 0)[0]:
-                        page = layer.pages[i]
-                        s = stager._slot(l & 1, n_staged)
-                        n_staged += 1
-                        slots[i] = s
-                        plan.setdefault(id(page.pool), (page.pool, [], []))
-                        plan[id(page.pool)][1].append(page.slot)
-                        plan[id(page.pool)][2].append(s)
-                        sig.append((page.page_id, page.generation))
-                tables[l, b, :n] = slots
-            plans.append(list(plan.values()))
+                tables[l, b, :n] = layer._slots[:n]
+                if not layer._cold:
+                    continue
+                cc = _cold_pages(layer)
+                k = len(cc.idx)
+                stage = _stage_slots(stager, parity, n_staged, n_staged + k)
+                tables[l, b, cc.idx] = stage
+                for pool, sel in cc.groups:
+                    g = groups.setdefault(id(pool), (pool, [], []))
+                    g[1].append(cc.host_slots[sel])
+                    g[2].append(stage[sel])
+                sig.append(cc.sig)
+                n_staged += k
+                n_cold += k
+                cold_bytes += cc.used_bytes
+            plans.append([(pool, np.concatenate(src), np.concatenate(dst))
+                          for pool, src, dst in groups.values()])
             cold_sig.append(tuple(sig))
+            if n_cold:   # same accounting as the eager path: one streamed call per layer
+                _record_prefetch(n_cold, cold_bytes)
+                self.h2d_bytes += n_cold * ctx.pool.page_bytes
         ctx.cold_plan = plans
-        h = ctx.host[ctx.flip]
-        if ctx.host_ev[ctx.flip] is not None:
-            ctx.host_ev[ctx.flip].synchronize()
-        hv = h.numpy()
-        o = 0
-        hv[o:o + rows.nbytes] = rows.view(np.uint8).reshape(-1)
-        o += rows.nbytes
-        hv[o:o + lens.nbytes] = lens.view(np.uint8).reshape(-1)
-        o += lens.nbytes
-        hv[o:o + tables.nbytes] = tables.view(np.uint8).reshape(-1)
-        ctx.blob.copy_(h, non_blocking=True)
+        ctx.blob.copy_(ctx.host[ctx.flip], non_blocking=True)
         ev = torch.cuda.Event()
         ev.record(torch.cuda.current_stream(self.dev))
         ctx.host_ev[ctx.flip] = ev
@@ -249,8 +302,9 @@ class GraphDecoder:
             if pool.capacity - pool.next_slot < 2 * pages + 16:
                 pool.reserve_capacity(2 * pages + 16)
             host = self.mgr.allocator.pool_for(torch.device("cpu"))
-            if host.capacity - host.next_slot < pages + 16:
-                host.reserve_capacity(pages + 16)
+            need = pages + self.L * B * ARENA_SLOTS   # a part-used arena per layer
+            if host.capacity - host.next_slot < need:
+                host.reserve_capacity(need)
         logits0 = loop.prefill(input_ids)
         self.ctx = _GraphContext(self.mgr, B, self.Hq, self.D, self.L, self.max_len, self.dtype,
                                  self.dev)
@@ -260,9 +314,17 @@ class GraphDecoder:
         history = torch.empty(B, max_new_tokens, dtype=torch.long, device=self.dev)
         history[:, 0] = self.ids[:, 0]
         all_logits = [logits0.float()] if keep_logits else None
+        # decode-phase timing (CUDA events around steps 1.., host planning time)
+        self.decode_events = (torch.cuda.Event(enable_timing=True),
+                              torch.cuda.Event(enable_timing=True))
+        self.plan_seconds = 0.0
+        self.h2d_bytes = 0
+        self.decode_events[0].record()
         # one eager step primes workspaces and attributes before any capture
         for step in range(1, max_new_tokens):
+            t0 = time.perf_counter()
             self._plan()
+            self.plan_seconds += time.perf_counter() - t0
             if self.graph is None or self._pending_sig != self.cold_sig:
                 if step == 1:
                     self._eager_step()
@@ -275,9 +337,15 @@ class GraphDecoder:
             history[:, step] = self.ids[:, 0]
             if keep_logits:
                 all_logits.append(self.logits.float().clone())
+        self.decode_events[1].record()
         out = (history, all_logits) if keep_logits else history
         self.graph = None   # captured pointers belong to this request
         return out
+
+    def decode_ms(self) -> float:
+        """Device time of the last generate's decode steps 1..n-1 (synchronises)."""
+        self.decode_events[1].synchronize()
+        return self.decode_events[0].elapsed_time(self.decode_events[1])
 
     def _eager_step(self) -> None:
         """The captured body run once without capture (same bookkeeping)."""

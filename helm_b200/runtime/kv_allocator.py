@@ -14,6 +14,11 @@ attention kernel addresses as base + slot * page_bytes.  KVPage.k_tensor /
 v_tensor are [1, H, P, D] views of the slot, exactly the reference's page
 shape.  Pools grow by doubling; a grown pool re-points the views of every
 live page (a caller holding an old view keeps reading the old storage).
+
+Slots are this module's own detail (the reference has none), so the host tier
+places evicted pages by layer: each layer fills an arena of ARENA_SLOTS
+consecutive slots in token order, and the cold pages of one layer then move to
+the device in a few long copies instead of one copy per page.
 """
 from __future__ import annotations
 
@@ -23,6 +28,7 @@ import torch
 
 _HOST_GROW_MIN = 16
 _DEVICE_GROW_MIN = 8
+ARENA_SLOTS = 64
 
 
 class PagePool:
@@ -41,19 +47,16 @@ class PagePool:
         self.pending_release: list[int] = []  # released once deferred copies are issued
         self.pages: dict[int, object] = {}    # slot -> page owning it (for re-pointing)
         self.staging: list[int] = []          # slots reserved for cold-page staging
+        self.page_bytes = 2 * num_kv_heads * page_size * head_dim * \
+            torch.tensor([], dtype=dtype).element_size()
+        self._arenas: dict = {}               # key -> (next slot, end) (host tier)
+        self._carve_from = 0
         if capacity > 0:
             self._resize(capacity)
 
     @property
     def is_host(self) -> bool:
         return self.device.type != "cuda"
-
-    @property
-    def page_bytes(self) -> int:
-        n = 1
-        for s in self.shape_tail:
-            n *= s
-        return n * torch.tensor([], dtype=self.dtype).element_size()
 
     def _alloc(self, capacity: int) -> torch.Tensor:
         shape = (capacity,) + self.shape_tail
@@ -85,17 +88,80 @@ class PagePool:
             self._resize(grow)
 
     def acquire(self, page) -> int:
-        if self.free_slots:
-            slot = self.free_slots.pop()
-        else:
+        slot = -1
+        while self.free_slots:
+            s = self.free_slots.pop()
+            if s not in self.pages:      # entries of slots an arena took since are stale
+                slot = s
+                break
+        if slot < 0:
             self.reserve_capacity(1)
             slot = self.next_slot
             self.next_slot += 1
+        self._bind(page, slot)
+        return slot
+
+    def _bind(self, page, slot: int) -> None:
         self.pages[slot] = page
         page.slot = slot
         page.k_tensor = self.storage[slot, 0].unsqueeze(0)
         page.v_tensor = self.storage[slot, 1].unsqueeze(0)
-        return slot
+
+    # -- per-layer arenas (host tier) -------------------------------------------
+    def place_in_arena(self, page, key) -> None:
+        """Re-binds a page just allocated as an eviction target to the next slot
+        of `key`'s arena (consecutive slots per layer, in eviction order)."""
+        nxt, end = self._arenas.get(key, (0, 0))
+        if nxt >= end or not self._takeable(nxt, page):
+            nxt = self._carve(page)
+            end = nxt + ARENA_SLOTS
+        self._rebind(page, nxt)
+        self._arenas[key] = (nxt + 1, end)
+
+    def forget_arenas(self, keys) -> None:
+        for k in keys:
+            self._arenas.pop(k, None)
+        if not self._arenas:
+            self._carve_from = 0
+
+    def _takeable(self, s: int, page) -> bool:
+        if s >= self.next_slot:
+            return True
+        owner = self.pages.get(s)
+        if owner is None:
+            return s not in self.staging
+        return owner is page or owner.state == "FREE"
+
+    def _carve(self, page) -> int:
+        """Start of ARENA_SLOTS consecutive takeable slots: the first such run at
+        or after the carve cursor, else fresh slots at the end of the pool."""
+        n = ARENA_SLOTS
+        run = 0
+        s = self._carve_from
+        while s < self.next_slot:
+            run = run + 1 if self._takeable(s, page) else 0
+            s += 1
+            if run == n:
+                self._carve_from = s
+                return s - n
+        start = self.next_slot - run
+        self.reserve_capacity(n - run)
+        self.next_slot = start + n
+        self._carve_from = self.next_slot
+        return start
+
+    def _rebind(self, page, s: int) -> None:
+        old = page.slot
+        if s == old:
+            return
+        owner = self.pages.get(s)
+        if owner is not None:          # a free page: the two trade slots
+            self._bind(owner, old)
+        else:
+            if self.pages.get(old) is page:
+                del self.pages[old]
+            self.free_slots.append(old)
+        self._bind(page, s)
 
     def release(self, slot: int, deferred: bool) -> None:
         self.pages.pop(slot, None)
@@ -135,6 +201,8 @@ class KVAllocator:
         self._next_page_id = 0
         self._pools: dict = {}
         self._initial = {"cuda": gpu_pool_pages, "cpu": cpu_pool_pages}
+        self._bpp_key = None
+        self._bpp = 0
         # When a list, GPU->CPU data copies are recorded here instead of being
         # issued (KVCacheManager defers them until the pages' data is written).
         self._deferred: Optional[list] = None
@@ -156,10 +224,18 @@ class KVAllocator:
     def pools(self):
         return list(self._pools.values())
 
+    def forget_arenas(self, keys) -> None:
+        keys = list(keys)
+        for pool in self._pools.values():
+            pool.forget_arenas(keys)
+
     @property
     def bytes_per_page(self) -> int:
-        return 2 * self.num_kv_heads * self.page_size * self.head_dim * \
-            torch.tensor([], dtype=self.dtype).element_size()
+        if self._bpp_key != self.dtype:
+            self._bpp = 2 * self.num_kv_heads * self.page_size * self.head_dim * \
+                torch.tensor([], dtype=self.dtype).element_size()
+            self._bpp_key = self.dtype
+        return self._bpp
 
     # --------------------------------------------------- reference API --
     def _create_page(self, device: torch.device):
@@ -219,15 +295,18 @@ class KVAllocator:
         else:
             self.cpu_free_pool.append(page)
 
-    def move_page(self, page, target_device: torch.device):
+    def move_page(self, page, target_device: torch.device, *, arena_key=None):
         """Moves a page to another tier (kv_allocator.py:95-144).  The data of the
         used tokens is copied by the copy engine on the current stream.  A GPU
         page that leaves for the host becomes DEAD and its slot returns to the
-        device pool (the reference frees its VRAM)."""
+        device pool (the reference frees its VRAM).  arena_key (not in the
+        reference): the host slot comes from that key's arena."""
         target_device = torch.device(target_device)
         if page.device == target_device:
             return page
         new_page = self.allocate(target_device)
+        if arena_key is not None and target_device.type != "cuda":
+            new_page.pool.place_in_arena(new_page, arena_key)
         used = page.used_tokens
         if used > 0:
             self._copy_page(new_page, page)

@@ -118,6 +118,7 @@ class LayerKVCache:
         self._n = 0
         self._ragged = False     # a page other than the last is not full
         self._cold = 0           # pages on the host tier
+        self._epoch = 0          # bumped whenever the table is re-derived
 
     def append_page(self, page: KVPage):
         self.pages.append(page)
@@ -744,7 +745,7 @@ class KVCacheManager:
             self._n_evictable -= 1
             original_start = page.start_token
             dev = page.device
-            new_page = self.allocator.move_page(page, torch.device("cpu"))
+            new_page = self.allocator.move_page(page, torch.device("cpu"), arena_key=id(layer))
             assert new_page.start_token == original_start, "Page invariant broken during migration"
             layer.pages[idx] = new_page
             if layer.tail_page is page:
@@ -772,6 +773,15 @@ class KVCacheManager:
         if gpu_bytes > self.gpu_high_watermark_bytes:
             self.evict_pages(gpu_bytes - self.gpu_high_watermark_bytes)
 
+    def _enforce_residency_tracked(self):
+        """The same policy for a caller that validated the tracking this step
+        (_tracking_ok) and has changed pages only through this manager since."""
+        if os.environ.get("HELM_B200_CHECK_RESIDENCY"):
+            return self._enforce_residency_policy()
+        gpu_bytes = self.allocator.bytes_per_page * self._n_evictable
+        if gpu_bytes > self.gpu_high_watermark_bytes:
+            self.evict_pages(gpu_bytes - self.gpu_high_watermark_bytes)
+
     # -- queries --------------------------------------------------------------
     def seq_len(self):
         if 0 in self.layers:
@@ -782,6 +792,7 @@ class KVCacheManager:
         return len(self.layers)
 
     def clear(self):
+        self.allocator.forget_arenas(id(L) for L in self.layers.values())
         for layer in self.layers.values():
             for page in layer.pages:
                 if page.state != "DEAD":
@@ -899,6 +910,7 @@ def _rebuild_table(layer: LayerKVCache) -> None:
     layer._n = 0
     layer._ragged = False
     layer._cold = 0
+    layer._epoch = getattr(layer, "_epoch", 0) + 1
     tail, pages = layer.tail_page, list(layer.pages)
     for p in pages:
         layer._track_new(p)

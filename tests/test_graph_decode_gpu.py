@@ -46,6 +46,10 @@ def test_graph_decode_matches_eager(model, watermark):
         gd = GraphDecoder(model, mgr, max_len=128 + n)
         toks_g, log_g = gd.generate(prompt, n, keep_logits=True)
         stats = get_paging_stats()
+        runs = []
+        for layer in mgr.kvcms[0].layers.values():   # host slots of a layer: few long runs
+            slots = [p.slot for p in layer.pages if p.state == "CPU"]
+            runs.append(1 + sum(b != a + 1 for a, b in zip(slots, slots[1:])) if slots else 0)
     finally:
         mgr.restore()
     assert torch.equal(toks_e, toks_g)
@@ -54,5 +58,6 @@ def test_graph_decode_matches_eager(model, watermark):
     if watermark is not None:
         assert stats["pages_evicted"] > 0
         assert gd.captures >= 2   # the cold set grew during decode
+        assert max(runs) == 1
     else:
         assert gd.captures == 1

@@ -87,6 +87,49 @@ def test_pool_growth_keeps_page_contents():
         assert torch.all(p.k_tensor == i)
 
 
+def test_host_arenas_give_each_layer_consecutive_slots():
+    """Eviction targets of interleaved layers land in per-layer runs of slots;
+    page ids and free lists are untouched; slots are reused after a reset."""
+    from helm_b200.runtime.kv_allocator import ARENA_SLOTS
+    a = _alloc()
+    pool = a.pool_for(CPU)
+    layers = 3
+    placed = {k: [] for k in range(layers)}
+    ids = []
+    for i in range(3 * ARENA_SLOTS):            # round-robin over layers, like evictions
+        page = a.allocate(CPU)
+        ids.append(page.page_id)
+        pool.place_in_arena(page, i % layers)
+        page.k_tensor.fill_(i)
+        placed[i % layers].append(page)
+    for pages in placed.values():
+        slots = [p.slot for p in pages]
+        assert slots == list(range(slots[0], slots[0] + len(slots)))
+    owners = {p.slot: p for ps in placed.values() for p in ps}
+    assert len(owners) == 3 * ARENA_SLOTS        # no slot given twice
+    for i, page in enumerate(p for k in range(layers) for p in placed[k]):
+        assert pool.pages[page.slot] is page
+        assert torch.all(page.k_tensor == pool.storage[page.slot, 0])
+    # reference page ids: batches of 16 created, popped last-first
+    assert ids == [16 * (i // 16) + 15 - i % 16 for i in range(3 * ARENA_SLOTS)]
+    top = pool.next_slot
+    for pages in placed.values():
+        for p in pages:
+            a.free(p)
+    a.forget_arenas(range(layers))
+    again = []
+    for i in range(2 * ARENA_SLOTS):             # allocate + place, as move_page does
+        again.append(a.allocate(CPU))
+        pool.place_in_arena(again[-1], 10 + i % 2)   # carved from the freed slots
+    assert pool.next_slot == top
+    for k in (0, 1):
+        slots = [p.slot for p in again[k::2]]
+        assert slots == list(range(slots[0], slots[0] + len(slots)))
+    assert len({p.slot for p in again}) == len(again)
+    spare = a.allocate(CPU)                       # plain allocations still get a free slot
+    assert spare.slot not in {p.slot for p in again}
+
+
 # ── cache manager (reference test_kv_cache.py) ─────────────────────────────────
 @pytest.fixture()
 def cache():
