@@ -211,6 +211,17 @@ def run_b200(args, rank: int, world: int, dev: torch.device):
     torch.cuda.synchronize(dev)
     if _capi.device_status(dev) != 0:
         raise RuntimeError("device status reported an error during warm-up")
+    # a decode step as the decode loop runs it: one CUDA graph replay (the
+    # decode kernel and its programmatically dependent merge kernel)
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            step()
+    stream.wait_stream(side)
+    graph.replay()
+    torch.cuda.synchronize(dev)
 
     def barrier():
         if world > 1:
@@ -227,12 +238,12 @@ def run_b200(args, rank: int, world: int, dev: torch.device):
         t_soak = time.perf_counter()
         while time.perf_counter() - t_soak < 0.6:
             for _ in range(50):
-                step()
+                graph.replay()
             torch.cuda.synchronize(dev)
         ev0.record(stream)
         for i in range(args.steps):
             per_step_events[i][0].record(stream)
-            step()
+            graph.replay()
             per_step_events[i][1].record(stream)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
@@ -306,13 +317,16 @@ def run_b200(args, rank: int, world: int, dev: torch.device):
                        B * 1e3 / (elapsed_ms / args.steps) * world},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "paged_decode_kernel (one launch per step; split-KV merge fused)",
+                     "kernel": "paged_decode_kernel + merge_split_pairs_kernel (PDL dependent); "
+                               "achieved = algorithmic bytes / time of the whole step",
                      "peak_source": peak_src,
                      "clock_note": "clocks sampled over a 0.6 s soak at the same load "
                                    "immediately before and during the timed region"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,
+        "execution": "value: CUDA graph replay of one decode call per step; e2e: eager calls "
+                     "through the C-ABI wrapper with host copies",
         "clocks": clocks.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -340,7 +354,7 @@ def run_seqsplit(args, rank: int, world: int, dev: torch.device):
     pt = torch.randperm(npg + 8, generator=g)[:npg].view(1, npg).to(torch.int32).to(dev)
     kl = torch.tensor([b - a], dtype=torch.int32, device=dev)
     q = torch.randn(Bq, Hq, Dh, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16).to(dev)
-    sp = SeqSplitAttention()
+    sp = SeqSplitAttention(exchange=args.exchange)
 
     def step():
         return sp.decode(q, pool, pt, kl, num_kv_heads=Hkv, page_size=Pg, scale=Dh ** -0.5,
@@ -380,6 +394,7 @@ def run_seqsplit(args, rank: int, world: int, dev: torch.device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item()) / args.steps
     del graph  # graphs holding NCCL calls go before the process group
+    sp.close()
     if _capi.device_status(dev) != 0:
         raise RuntimeError("device status reported an error")
     if rank == 0:
@@ -388,13 +403,18 @@ def run_seqsplit(args, rank: int, world: int, dev: torch.device):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": "seqsplit128k: configs[3] attention, B=1, 40q/8kv, D=128, "
-                                       "T=131072, 16-token pages, split over the GPUs, NCCL "
-                                       "all-gather of fp32 (O, LSE) + merge",
+                                       "T=131072, 16-token pages, split over the GPUs, fp32 "
+                                       "(O, LSE) exchanged and merged "
+                                       + ("by one peer-memory kernel over NVLink"
+                                          if args.exchange == "p2p" else
+                                          "by NCCL all-gather + merge kernel"),
+                           "exchange": args.exchange if world > 1 else "none (1 GPU)",
                            "tokens_per_gpu": b - a, "algorithmic_bytes_per_step": alg,
                            "attention_calls_per_s_one_layer": 1e3 / ms,
                            "parallelism": f"sequence split x{world}",
                            "execution": "CUDA graph replay of the whole step"},
-                "gpu_launches": args.steps * 2, "clocks": clocks.summary()}
+                "gpu_launches": args.steps * (1 if world == 1 else 2),
+                "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
 
 
@@ -532,6 +552,8 @@ def main():
                     help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
                          "configs[3] split across the GPUs (strong scaling); or whole-model "
                          "decode tok/s of configs[0] (config1) / configs[2] (config3)")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="seqsplit128k: how partial states cross GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-len", type=int, default=T,
                     help="tokens per sequence (profiling a smaller case only)")

@@ -55,6 +55,16 @@ _SIGNATURES = {
     "helm_copy_pages": (_I, [_P, _P, _I64, _P, _P, _I64, _P]),
     "helm_gather_kv": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     "helm_merge_attention_states": (_I, [_P, _I, _I64, _P, _I64, _I, _I64, _I, _P, _I, _P, _P]),
+    "helm_peer_exchange_bytes": (_I64, [_I64, _I, _I]),
+    "helm_ipc_alloc": (_I, [_I64, ctypes.POINTER(_P)]),
+    "helm_ipc_free": (_I, [_P]),
+    "helm_ipc_zero": (_I, [_P, _I64, _P]),
+    "helm_ipc_handle_bytes": (_I, []),
+    "helm_ipc_get_handle": (_I, [_P, _P]),
+    "helm_ipc_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "helm_ipc_close": (_I, [_P]),
+    "helm_seq_exchange_merge": (_I, [_P, _I, _I, _P, _P, _I64, _I, _P, _I, _P,
+                                     ctypes.c_uint64, _P]),
 }
 
 _lib = None
@@ -127,8 +137,7 @@ def _stream_handle(device: torch.device, stream=None) -> int:
 
 def device_status(device: torch.device, reset: bool = True, stream=None) -> int:
     """Synchronises `stream` and returns the device status word (HELM_DEV_* bits).
-    A non-zero word also re-zeroes the decode workspace counters, which an
-    abandoned call may have left set."""
+    A non-zero word also zeroes the decode workspace."""
     out = ctypes.c_uint(0)
     with torch.cuda.device(device):
         _check(lib().helm_get_device_status(ctypes.byref(out), int(reset),
@@ -141,41 +150,35 @@ def device_status(device: torch.device, reset: bool = True, stream=None) -> int:
 
 # ------------------------------------------------------------------ workspace --
 class _Workspace:
-    """Per-device scratch of the decode kernel: per-pair counters (must be zero
-    at call start; a completed call leaves them zero) then fp32 partials."""
+    """Per-device scratch of the decode kernel (fp32 split-KV partials; needs
+    no initialisation).  Grows, never shrinks."""
 
     def __init__(self):
         self.buf: Optional[torch.Tensor] = None
-        self.clean_counter_bytes = 0   # prefix known to be zero
 
-    def get(self, device: torch.device, nbytes: int, counter_bytes: int) -> torch.Tensor:
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
         if self.buf is None or self.buf.numel() < nbytes:
             self.buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-            self.clean_counter_bytes = self.buf.numel()
-        if counter_bytes > self.clean_counter_bytes:
-            self.buf[:counter_bytes].zero_()
-        # partials of this call start right after its counters
-        self.clean_counter_bytes = counter_bytes
         return self.buf
 
 
 _workspaces: dict = {}
 
 
-def _workspace(device: torch.device, nbytes: int, counter_bytes: int) -> torch.Tensor:
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     key = (device.type, device.index)
     ws = _workspaces.get(key)
     if ws is None:
         ws = _workspaces[key] = _Workspace()
-    return ws.get(device, nbytes, counter_bytes)
+    return ws.get(device, nbytes)
 
 
 def reset_workspace(device: torch.device) -> None:
-    """Re-zeroes the counters, e.g. after a call that reported an error."""
+    """Zeroes the workspace (nothing depends on it; kept for callers that
+    clean up after an error)."""
     ws = _workspaces.get((device.type, device.index))
     if ws is not None and ws.buf is not None:
         ws.buf.zero_()
-        ws.clean_counter_bytes = ws.buf.numel()
 
 
 def decode_workspace_bytes(device: torch.device, batch: int, hq: int, hkv: int, d: int) -> int:
@@ -217,7 +220,7 @@ def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torc
     if out.dtype not in (q.dtype, torch.float32) or out.stride(2) != 1:
         raise HelmError("out must be [B, Hq, D] in the query dtype or fp32, unit dim stride")
     ws_bytes = decode_workspace_bytes(dev, B, Hq, num_kv_heads, D)
-    ws = _workspace(dev, ws_bytes, ((4 * B * num_kv_heads + 255) // 256) * 256)
+    ws = _workspace(dev, ws_bytes)
     mask_ptr, mask_dt, mask_sb = None, 0, 0
     if mask is not None:
         if mask.stride(-1) != 1:
@@ -332,3 +335,73 @@ def merge_attention_states(o_parts: torch.Tensor, lse_parts: torch.Tensor,
             out.data_ptr(), helm_dtype(out_dtype), lse.data_ptr(), _stream_handle(dev, stream))
     _check(rc, "helm_merge_attention_states")
     return out, lse
+
+
+# ── peer-memory exchange (sequence split) ─────────────────────────────────────
+def peer_exchange_bytes(rows: int, head_dim: int, world: int) -> int:
+    n = lib().helm_peer_exchange_bytes(rows, head_dim, world)
+    if n < 0:
+        raise HelmError(f"unsupported exchange geometry rows={rows} head_dim={head_dim} "
+                        f"world={world}")
+    return int(n)
+
+
+def ipc_alloc(nbytes: int, device: torch.device) -> int:
+    p = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        _check(lib().helm_ipc_alloc(nbytes, ctypes.byref(p)), "helm_ipc_alloc")
+    return int(p.value)
+
+
+def ipc_free(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _check(lib().helm_ipc_free(ptr), "helm_ipc_free")
+
+
+def ipc_zero(ptr: int, nbytes: int, device: torch.device, stream=None) -> None:
+    with torch.cuda.device(device):
+        _check(lib().helm_ipc_zero(ptr, nbytes, _stream_handle(device, stream)), "helm_ipc_zero")
+
+
+def ipc_get_handle(ptr: int, device: torch.device) -> bytes:
+    buf = ctypes.create_string_buffer(lib().helm_ipc_handle_bytes())
+    with torch.cuda.device(device):
+        _check(lib().helm_ipc_get_handle(ptr, buf), "helm_ipc_get_handle")
+    return buf.raw
+
+
+def ipc_open(handle: bytes, device: torch.device) -> int:
+    p = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        _check(lib().helm_ipc_open(handle, ctypes.byref(p)), "helm_ipc_open")
+    return int(p.value)
+
+
+def ipc_close(ptr: int, device: torch.device) -> None:
+    with torch.cuda.device(device):
+        _check(lib().helm_ipc_close(ptr), "helm_ipc_close")
+
+
+def seq_exchange_merge(bufs: list, rank: int, o_part: torch.Tensor, lse_part: torch.Tensor,
+                       out: torch.Tensor, lse_out: Optional[torch.Tensor] = None,
+                       timeout_s: float = 5.0, stream=None) -> None:
+    """Exchange + merge of partial states over peer memory: o_part fp32
+    [rows, D], lse_part fp32 [rows] -> out [rows, D] (its dtype), lse_out."""
+    D = o_part.shape[-1]
+    rows = lse_part.numel()
+    if o_part.dtype != torch.float32 or lse_part.dtype != torch.float32:
+        raise HelmError("partial states must be fp32")
+    if not (o_part.is_contiguous() and lse_part.is_contiguous() and out.is_contiguous()):
+        raise HelmError("o_part, lse_part and out must be contiguous")
+    if o_part.numel() != rows * D or out.numel() != rows * D:
+        raise HelmError("o_part / out must hold rows * head_dim elements")
+    if lse_out is not None and (lse_out.dtype != torch.float32 or lse_out.numel() != rows):
+        raise HelmError("lse_out must be fp32 [rows]")
+    dev = o_part.device
+    arr = (ctypes.c_void_p * len(bufs))(*bufs)
+    with torch.cuda.device(dev):
+        rc = lib().helm_seq_exchange_merge(arr, rank, len(bufs), o_part.data_ptr(),
+                                           lse_part.data_ptr(), rows, D, out.data_ptr(),
+                                           helm_dtype(out.dtype), _ptr(lse_out),
+                                           int(timeout_s * 1e9), _stream_handle(dev, stream))
+    _check(rc, "helm_seq_exchange_merge")

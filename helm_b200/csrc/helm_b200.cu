@@ -9,6 +9,7 @@
 #include "kv_ops.cu"
 #include "paged_attention.cu"
 #include "paged_attention_noalloc.cu"
+#include "peer_exchange.cu"
 
 namespace helm {
 

@@ -13,9 +13,12 @@
 // current pair, and when its range leaves a pair either writes the final
 // output (it covered the whole pair) or an fp32 partial state (m, l,
 // unnormalised O) at the unique slot worker + pair.  After its loop, a CTA
-// bumps a per-pair counter for every split pair it touched; the CTA that
-// completes the count merges that pair's partials with all its consumer
-// warps and resets the counter (no second kernel, no spin-wait).
+// combines the states of its warps that end in the same pair: the final
+// output when the CTA covered the whole pair, else one CTA partial.  A second
+// kernel, launched as a programmatic dependent (its CTAs are placed while the
+// first still runs and wait in griddepcontrol.wait), merges the pairs split
+// across CTAs, every split pair at once, each thread with the loads of all
+// its sources in flight together.
 //
 // Per CTA: one producer warp issues TMA tile loads (two 64-column boxes per K
 // or V tile, 128-byte swizzled so ldmatrix reads are bank-conflict free) into
@@ -62,7 +65,6 @@ struct DecodeArgs {
   float* part_ml;   // warp partials [num_workers + pairs][G][2]  (m in log2 units, l)
   float* cta_o;     // CTA partials [grid + pairs][G][D]
   float* cta_ml;    // CTA partials [grid + pairs][G][2]
-  int* counters;    // [B * Hkv] CTAs done per pair; zero between calls
   int batch, hq, hkv, group, page_size, tiles_per_page;
   int out_fp32;  // O written as fp32 (partial states for a cross-device merge)
   float scale;
@@ -544,84 +546,6 @@ __device__ void merge_sources(const DecodeArgs& a, int p, const float* s_states,
   consumer_barrier(kConsumers);
 }
 
-// One cross-CTA merge job: pair p, CTA partials at slots c0..c0+n_cta-1 (+p),
-// and the warp partial at slot warp_slot+p when warp_slot >= 0.
-struct MergeJob {
-  int p, c0, n_cta, warp_slot;
-};
-
-constexpr int kMaxDirectSources = 8;
-
-// Finishes several split pairs at once.  Each thread owns output elements
-// (job, head, dim) and loads the (m, l) and O value of every source of its
-// element together, so a job costs one dependent L2 round trip.  Jobs with
-// more than kMaxDirectSources sources are left to merge_sources.
-template <typename T, int D, int NCW>
-__device__ void merge_global(const DecodeArgs& a, const MergeJob* jobs, int n_jobs) {
-  constexpr int kConsumers = NCW * 32;
-  constexpr int kElems = 4;  // output elements per thread whose loads are in flight together
-  const int G = a.group;
-  const int per_job = G * D;
-  const int n_elem = n_jobs * per_job;
-  for (int e0 = 0; e0 < n_elem; e0 += kConsumers * kElems) {
-    float2 ml[kElems][kMaxDirectSources];
-    float o[kElems][kMaxDirectSources];
-    int K[kElems], hg[kElems], d[kElems], j[kElems];
-#pragma unroll
-    for (int i = 0; i < kElems; ++i) {
-      const int e = e0 + i * kConsumers + threadIdx.x;
-      K[i] = 0;
-      j[i] = 0;
-      hg[i] = 0;
-      d[i] = 0;
-      if (e < n_elem) {
-        j[i] = e / per_job;
-        const int r = e - j[i] * per_job;
-        hg[i] = r / D;
-        d[i] = r - hg[i] * D;
-        const MergeJob job = jobs[j[i]];
-        K[i] = job.n_cta + (job.warp_slot >= 0 ? 1 : 0);
-        if (K[i] > kMaxDirectSources) K[i] = 0;  // left to merge_sources
-      }
-#pragma unroll
-      for (int k = 0; k < kMaxDirectSources; ++k) {
-        ml[i][k] = make_float2(-INFINITY, 0.f);
-        o[i][k] = 0.f;
-        if (k < K[i]) {
-          const MergeJob job = jobs[j[i]];
-          const int64_t slot = k < job.n_cta ? static_cast<int64_t>(job.c0 + k + job.p)
-                                             : static_cast<int64_t>(job.warp_slot + job.p);
-          const float* mlp = (k < job.n_cta ? a.cta_ml : a.part_ml) + (slot * G + hg[i]) * 2;
-          const float* op = (k < job.n_cta ? a.cta_o : a.part_o) + (slot * G + hg[i]) * D + d[i];
-          ml[i][k] = __ldcg(reinterpret_cast<const float2*>(mlp));
-          o[i][k] = __ldcg(op);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kElems; ++i) {
-      if (K[i] == 0) continue;
-      float M = -INFINITY;
-#pragma unroll
-      for (int k = 0; k < kMaxDirectSources; ++k) M = fmaxf(M, ml[i][k].x);
-      const float m_use = M == -INFINITY ? 0.f : M;
-      float L = 0.f, acc = 0.f;
-#pragma unroll
-      for (int k = 0; k < kMaxDirectSources; ++k) {
-        const float w = k < K[i] ? exp2f(ml[i][k].x - m_use) : 0.f;
-        L += ml[i][k].y * w;
-        acc += o[i][k] * w;
-      }
-      const int p = jobs[j[i]].p;
-      const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
-      store_out<T>(a, b, h * G + hg[i], d[i], acc / fmaxf(L, 1e-12f));
-      if (d[i] == 0 && a.lse != nullptr)
-        a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg[i]] =
-            (M == -INFINITY || L <= 0.f) ? -INFINITY : M * kLn2 + logf(L);
-    }
-  }
-}
-
 template <int D>
 struct Layout {
   static constexpr int NCW = D <= 128 ? 8 : 4;  // consumer warps (= workers) per CTA
@@ -664,6 +588,8 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     s_abort = 0;
   }
   __syncthreads();
+  // the merge kernel may be placed now; it waits for this grid to complete
+  asm volatile("griddepcontrol.launch_dependents;");
 
   // Pairs without tokens: zero output, LSE = -inf.
   for (int p = blockIdx.x; p < a.batch * a.hkv; p += gridDim.x) {
@@ -790,9 +716,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   //    goes to a shared-memory record (the tile ring is idle now);
   // 2. warps of this CTA ending in the same pair are combined: the final
   //    output when this CTA covers the whole pair, else one CTA partial;
-  // 3. for pairs split across CTAs, every CTA touching the pair bumps its
-  //    counter after writing; the CTA that completes the count merges the
-  //    CTA partials (plus the mid-range warp partial, if any) and resets it.
+  // 3. pairs split across CTAs are merged by merge_split_pairs_kernel.
   constexpr int kRec = 32 + 16 * D;
   float* s_states = reinterpret_cast<float*>(smem);
   float* s_scratch = s_states + NCW * kRec;
@@ -830,50 +754,91 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     }
     w0 = w1;
   }
-  // (merge_sources ends with a barrier; the counter atomic below releases the
-  //  partials written by this CTA's threads, warp partials included)
-  const int x0 = v0 * W, x1 = min((v0 + NCW) * W, total);
-  const TilePos pf = locate(s_cum, a.batch, a.hkv, x0);
-  const TilePos pl = locate(s_cum, a.batch, a.hkv, x1 - 1);
-  const int p_first = pf.b * a.hkv + pf.h, p_last = pl.b * a.hkv + pl.h;
-  // Counter bumps for every split pair this CTA touched, all in flight at
-  // once; the pairs whose count this CTA completes become merge jobs.
-  MergeJob* s_jobs = reinterpret_cast<MergeJob*>(s_scratch);
-  __shared__ int s_njobs;
-  for (int base = p_first; base <= p_last; base += kConsumers) {
-    if (threadIdx.x == 0) s_njobs = 0;
-    consumer_barrier(kConsumers);
-    const int p = base + threadIdx.x;
-    if (p <= p_last) {
-      const PairSpan ps = pair_span(a, s_cum, W, total, p);
-      const int cf = ps.vf / NCW, cl = ps.vl / NCW;
-      if (ps.tiles > 0 && ps.vf != ps.vl && cf != cl) {
-        if (atomic_add_acq_rel_gpu(a.counters + p, 1) == cl - cf) {
-          const int vl_end = ps.last_continues ? ps.vl - 1 : ps.vl;
-          MergeJob job;
-          job.p = p;
-          job.c0 = ps.vf / NCW;
-          job.n_cta = vl_end / NCW - job.c0 + 1;
-          job.warp_slot = ps.last_continues ? ps.vl : -1;
-          s_jobs[atomicAdd(&s_njobs, 1)] = job;
-          a.counters[p] = 0;  // ready for the next call
-        }
+}
+
+// Merges the pairs whose tiles were split across CTAs (second kernel of a
+// call).  CTA (pair p, chunk) owns up to kMergeThreads float4 elements of p's
+// G x D output block.  Its sources are the CTA partials of CTAs
+// vf/NCW .. vl_end/NCW (slots c + p) and, when the pair's last worker
+// continues into the next pair, that worker's partial (slot vl + p).  Each
+// thread loads (m, l) and O of up to kMergeBatch sources at once, rescaling
+// its running state between batches, so a pair costs one dependent L2 round
+// trip per kMergeBatch sources.
+constexpr int kMergeThreads = 128;
+constexpr int kMergeBatch = 16;
+
+template <typename T, int D, int NCW>
+__global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const DecodeArgs a) {
+  extern __shared__ int s_cum_m[];
+  const int p = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (warp == 0) build_prefix(a, s_cum_m, lane);
+  __syncthreads();
+  const int total = s_cum_m[a.batch] * a.hkv;
+  if (total == 0) return;
+  const int W = div_up(total, a.num_workers);
+  const PairSpan ps = pair_span(a, s_cum_m, W, total, p);
+  if (ps.tiles == 0 || ps.vf == ps.vl || ps.vf / NCW == ps.vl / NCW) return;  // not split
+  const int vl_end = ps.last_continues ? ps.vl - 1 : ps.vl;
+  const int c0 = ps.vf / NCW, n_cta = vl_end / NCW - c0 + 1;
+  const int K = n_cta + (ps.last_continues ? 1 : 0);
+  const int G = a.group;
+  constexpr int D4 = D / 4;
+  const int e = blockIdx.y * kMergeThreads + threadIdx.x;
+  if (e >= G * D4) return;
+  const int hg = e / D4, d4 = e - (e / D4) * D4;
+  // the decode kernel's partials are complete and visible after this
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  float M = -INFINITY, Lsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k0 = 0; k0 < K; k0 += kMergeBatch) {
+    float2 ml[kMergeBatch];
+    float4 o[kMergeBatch];
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {  // issue the whole batch first
+      const int k = k0 + i;
+      ml[i] = make_float2(-INFINITY, 0.f);
+      o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < K) {
+        const bool cta_src = k < n_cta;
+        const int64_t slot = cta_src ? static_cast<int64_t>(c0 + k + p)
+                                     : static_cast<int64_t>(ps.vl + p);
+        const float* mlp = (cta_src ? a.cta_ml : a.part_ml) + (slot * G + hg) * 2;
+        const float* op = (cta_src ? a.cta_o : a.part_o) + (slot * G + hg) * D + d4 * 4;
+        ml[i] = __ldcg(reinterpret_cast<const float2*>(mlp));
+        o[i] = __ldcg(reinterpret_cast<const float4*>(op));
       }
     }
-    consumer_barrier(kConsumers);
-    const int n_jobs = s_njobs;
-    if (n_jobs > 0) {
-      merge_global<T, D, NCW>(a, s_jobs, n_jobs);
-      // jobs with too many sources for the one-pass merge
-      for (int j = 0; j < n_jobs; ++j) {
-        const MergeJob job = s_jobs[j];
-        if (job.n_cta + (job.warp_slot >= 0 ? 1 : 0) > kMaxDirectSources)
-          merge_sources<T, D, NCW>(a, job.p, s_states, 0, 0, job.c0, job.n_cta, job.warp_slot,
-                                   true, 0, s_scratch + 4 * kConsumers);
-      }
+    float Mb = M;
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) Mb = fmaxf(Mb, ml[i].x);
+    if (Mb == -INFINITY) continue;  // no valid token in any source so far
+    const float r = exp2f(M - Mb);   // 0 while M is -inf
+    Lsum *= r;
+    acc.x *= r;
+    acc.y *= r;
+    acc.z *= r;
+    acc.w *= r;
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) {
+      const float w = exp2f(ml[i].x - Mb);
+      Lsum += ml[i].y * w;
+      acc.x += w * o[i].x;
+      acc.y += w * o[i].y;
+      acc.z += w * o[i].z;
+      acc.w += w * o[i].w;
     }
-    consumer_barrier(kConsumers);
+    M = Mb;
   }
+  const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
+  const float inv = 1.f / fmaxf(Lsum, 1e-12f);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 0, acc.x * inv);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 1, acc.y * inv);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 2, acc.z * inv);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 3, acc.w * inv);
+  if (d4 == 0 && a.lse != nullptr)
+    a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg] =
+        (M == -INFINITY || Lsum <= 0.f) ? -INFINITY : M * kLn2 + logf(Lsum);
 }
 
 // ----------------------------------------------------------------- host side --
@@ -931,6 +896,20 @@ int launch(const DecodeArgs& a, const void* pool, int64_t pool_rows, int grid,
   paged_decode_kernel<T, D, NT>
       <<<grid, L::kThreads, L::smem_bytes(a.batch), stream>>>(map, args);
   if (cudaGetLastError() != cudaSuccess) return HELM_ERR_CUDA;
+  // merge of split pairs: a programmatic dependent of the decode kernel
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.hkv),
+                     static_cast<unsigned>((a.group * (D / 4) + kMergeThreads - 1) / kMergeThreads));
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(a.batch + 1) * sizeof(int);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, merge_split_pairs_kernel<T, D, L::NCW>, args) != cudaSuccess)
+    return HELM_ERR_CUDA;
   return HELM_OK;
 }
 
@@ -962,10 +941,10 @@ int64_t paged_decode_slots(int batch, int num_kv_heads) {
          static_cast<int64_t>(batch) * num_kv_heads;
 }
 
-// Workspace: per-pair counters [B*Hkv] int32 | partial O [slots][G][D] fp32 |
+// Workspace: reserved [B*Hkv] int32 (kept zero) | partial O [slots][G][D] fp32 |
 // partial (m, l) [slots][G][2] fp32, each region 256-byte aligned.  The
-// counters (the first roundup(4*B*Hkv, 256) bytes) must be zero when a call
-// starts; a call that completes leaves them zero.
+// reserved region (the first roundup(4*B*Hkv, 256) bytes) is neither read
+// nor written.
 struct WorkspaceLayout {
   int64_t cnt_bytes, o_bytes, ml_bytes, cta_o_bytes, cta_ml_bytes;
   WorkspaceLayout(int batch, int hq, int hkv, int d) {
@@ -1053,7 +1032,6 @@ extern "C" int helm_paged_decode_attention(
   a.out_sh = out_stride_h;
   a.lse = lse;
   uint8_t* wsp = static_cast<uint8_t*>(workspace);
-  a.counters = reinterpret_cast<int*>(wsp);
   a.part_o = reinterpret_cast<float*>(wsp + ws.cnt_bytes);
   a.part_ml = reinterpret_cast<float*>(wsp + ws.cnt_bytes + ws.o_bytes);
   a.cta_o = reinterpret_cast<float*>(wsp + ws.cnt_bytes + ws.o_bytes + ws.ml_bytes);

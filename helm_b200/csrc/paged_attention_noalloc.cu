@@ -1,7 +1,7 @@
 // Decode attention for callers that cannot allocate device memory.
 //
 // helm_paged_decode_attention needs a scratch workspace (split-KV partial
-// softmax states plus per-pair counters) that its caller allocates.  Some
+// softmax states) that its caller allocates.  Some
 // callers cannot do that: a serving process that hands all of HBM to its own
 // page pool at start-up, so any later cudaMalloc fails or fragments that pool;
 // or a decode loop that must not stall on the device-wide synchronisation that
@@ -20,9 +20,9 @@
 //  * Every call uses the same array.  Calls that overlap on the GPU (different
 //    streams, or different host threads without ordering) race on it and give
 //    wrong results; order them on one stream.
-//  * The per-pair counters at the start of the array are cleared on the
-//    caller's stream at every call, so a call never depends on what an earlier
-//    call (or an abandoned one) left behind.
+//  * Nothing in the array has to start at zero: every value a call reads was
+//    written earlier in the same call, so a call never depends on what an
+//    earlier (or an abandoned) call left behind.
 #include "common.cuh"
 
 namespace helm {
@@ -69,14 +69,6 @@ extern "C" int helm_paged_decode_attention_noalloc(
       return HELM_ERR_CUDA;
     }
     g_noalloc_scratch_addr[dev] = scratch;
-  }
-  // The kernel needs zeroed per-pair counters at the start of the scratch.
-  const int64_t counter_bytes = ((4 * int64_t(batch) * num_kv_heads + 255) / 256) * 256;
-  e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(counter_bytes),
-                      static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) {
-    set_last_cuda_error(e);
-    return HELM_ERR_CUDA;
   }
   return helm_paged_decode_attention(
       q, q_stride_b, q_stride_h, kv_pool, pool_pages, page_table, pt_stride_b, max_pages, kv_lens,

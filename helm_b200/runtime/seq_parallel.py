@@ -7,8 +7,11 @@ multi-GPU forms of its decode attention:
 Sequence split (long contexts).  Rank r of N holds a contiguous, page-aligned
 token range of every sequence in its own page pool.  Each decode step it
 computes the partial attention state of its range with the paged decode
-kernel (O in fp32 and LSE), the N states are all-gathered in one packed
-buffer over NCCL (NVLink/NVSwitch), and every rank merges them:
+kernel (O in fp32 and LSE); one native kernel then pushes the state to every
+rank over NVLink (CUDA IPC mappings of per-rank exchange buffers), waits for
+the other ranks' states and merges them (PeerExchange).  The NCCL form --
+all-gather of the packed states, then the merge kernel -- is kept for
+process groups without peer mappings (and gloo on CPU).  The merge is
 
     M = max_r LSE_r,  O = sum_r e^(LSE_r - M) O_r / sum_r e^(LSE_r - M)
 
@@ -49,6 +52,57 @@ def head_range(num_kv_heads: int, num_q_heads: int, rank: int, world: int):
     return kv, (kv[0] * group, kv[1] * group)
 
 
+class PeerExchange:
+    """Per-rank exchange buffers mapped into every rank (CUDA IPC), for
+    helm_seq_exchange_merge.  Collective: every rank of `group` constructs it
+    with the same rows / head_dim and calls merge() the same number of times."""
+
+    def __init__(self, rows: int, head_dim: int, device: torch.device,
+                 group: Optional[dist.ProcessGroup] = None, timeout_s: float = 5.0):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.rows, self.head_dim, self.device = rows, head_dim, torch.device(device)
+        self.timeout_s = timeout_s
+        self.nbytes = _capi.peer_exchange_bytes(rows, head_dim, self.world)
+        self.local = _capi.ipc_alloc(self.nbytes, self.device)
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, _capi.ipc_get_handle(self.local, self.device),
+                                   group=group)
+        self.ptrs = [self.local if r == self.rank else _capi.ipc_open(handles[r], self.device)
+                     for r in range(self.world)]
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def merge(self, o_part: torch.Tensor, lse_part: torch.Tensor, out: torch.Tensor,
+              lse_out: Optional[torch.Tensor] = None, stream=None) -> None:
+        _capi.seq_exchange_merge(self.ptrs, self.rank, o_part, lse_part, out, lse_out,
+                                 timeout_s=self.timeout_s, stream=stream)
+
+    def reset(self) -> None:
+        """Re-zeroes this rank's buffer (all ranks, e.g. after a timeout)."""
+        torch.cuda.synchronize(self.device)
+        _capi.ipc_zero(self.local, self.nbytes, self.device)
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        if self.ptrs is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)     # no rank still writes into a buffer
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                _capi.ipc_close(p, self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)     # every mapping of this buffer is closed
+        _capi.ipc_free(self.local, self.device)
+        self.ptrs = None
+
+
 class SeqSplitAttention:
     """Merged decode attention over a sequence split across the ranks of `group`.
 
@@ -60,10 +114,26 @@ class SeqSplitAttention:
     """
 
     def __init__(self, group: Optional[dist.ProcessGroup] = None,
-                 merge_fn: Optional[Callable] = None):
+                 merge_fn: Optional[Callable] = None, exchange: str = "p2p"):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.merge_fn = merge_fn or _capi.merge_attention_states
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError("exchange must be 'p2p' or 'nccl'")
+        self.exchange_kind = exchange
+        self._peers: dict = {}
+
+    def peer_exchange(self, rows: int, head_dim: int, device) -> PeerExchange:
+        key = (rows, head_dim, torch.device(device))
+        px = self._peers.get(key)
+        if px is None:
+            px = self._peers[key] = PeerExchange(rows, head_dim, device, self.group)
+        return px
+
+    def close(self) -> None:
+        for px in self._peers.values():
+            px.close()
+        self._peers.clear()
 
     def exchange(self, part: torch.Tensor) -> torch.Tensor:
         """All-gathers this rank's packed state [rows*(D+1)] -> [world, rows*(D+1)]."""
@@ -91,12 +161,25 @@ class SeqSplitAttention:
         LSE fp32 [B, Hq]) of attention over all ranks' ranges."""
         B, Hq, D = q.shape
         rows = B * Hq
+        if self.world == 1 and q.device.type == "cuda":   # nothing to exchange
+            lse = torch.empty(B, Hq, dtype=torch.float32, device=q.device)
+            out, _ = _capi.paged_decode_attention(q, pool, page_table, kv_lens,
+                                                  num_kv_heads=num_kv_heads, page_size=page_size,
+                                                  scale=scale, softcap=softcap, mask=mask, lse=lse,
+                                                  max_kv_len_hint=max_kv_len_hint)
+            return out, lse
         part = torch.empty(rows * (D + 1), dtype=torch.float32, device=q.device)
         o_local = part[:rows * D].view(B, Hq, D)
         lse_local = part[rows * D:].view(B, Hq)
         _capi.paged_decode_attention(q, pool, page_table, kv_lens, num_kv_heads=num_kv_heads,
                                      page_size=page_size, scale=scale, softcap=softcap, mask=mask,
                                      out=o_local, lse=lse_local, max_kv_len_hint=max_kv_len_hint)
+        if self.exchange_kind == "p2p" and q.device.type == "cuda" and self.world > 1:
+            out = torch.empty(B, Hq, D, dtype=q.dtype, device=q.device)
+            lse = torch.empty(B, Hq, dtype=torch.float32, device=q.device)
+            self.peer_exchange(rows, D, q.device).merge(o_local.view(rows, D), lse_local.view(rows),
+                                                        out, lse)
+            return out, lse
         gathered = self.exchange(part)
         out, lse = self.merge(gathered, rows, D, q.dtype)
         return out.view(B, Hq, D), lse.view(B, Hq)

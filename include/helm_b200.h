@@ -94,12 +94,11 @@ int64_t helm_paged_decode_workspace_bytes(int batch, int num_q_heads, int num_kv
  *               query dtype, or HELM_DTYPE_FP32 (partial states that another
  *               device's results are merged with, see helm_merge_attention_states)
  *  lse          optional fp32 [B, Hq]
- *  workspace    >= helm_paged_decode_workspace_bytes(...) bytes, 256-byte aligned.
- *               Its first roundup(4*batch*num_kv_heads, 256) bytes are per-pair
- *               counters that must be zero when the call starts (zero-fill a
- *               new workspace); a call that completes leaves them zero, but the
- *               bytes after them are overwritten, so re-zero that prefix when
- *               a call uses a larger batch*num_kv_heads than the previous one.
+ *  workspace    >= helm_paged_decode_workspace_bytes(...) bytes, 256-byte aligned,
+ *               holding the split-KV partial states; no initialisation needed
+ *               (its first roundup(4*batch*num_kv_heads, 256) bytes are reserved).
+ *               The call launches two kernels on `stream`: the decode kernel and,
+ *               as its programmatic dependent, the merge of split pairs.
  *  max_kv_len_hint  upper bound on kv_lens (0 = unknown); sizes the grid
  */
 int helm_paged_decode_attention(const void* q, int64_t q_stride_b, int64_t q_stride_h,
@@ -127,8 +126,8 @@ int helm_paged_decode_attention(const void* q, int64_t q_stride_b, int64_t q_str
  * helm_paged_decode_workspace_bytes) return HELM_ERR_WORKSPACE.  The first call
  * on a device sets up that device's scratch address: make it before any stream
  * capture.  All calls share the array, so calls that overlap on the GPU race;
- * keep them ordered on one stream.  Each call clears the counters it needs on
- * `stream` first and allocates nothing.
+ * keep them ordered on one stream.  Nothing in the array needs to start at
+ * zero, and a call allocates nothing.
  */
 int helm_paged_decode_attention_noalloc(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                                         const void* kv_pool, int64_t pool_pages,
@@ -221,6 +220,45 @@ int helm_merge_attention_states(const void* o_parts, int o_dtype, int64_t o_part
                                 const float* lse_parts, int64_t lse_part_stride, int num_parts,
                                 int64_t rows, int head_dim, void* out, int out_dtype,
                                 float* lse_out, void* stream);
+
+/*
+ * Sequence-split exchange over peer memory (one process per GPU, one node).
+ *
+ * helm_ipc_alloc      cudaMalloc + zero fill of an exchange buffer on the
+ *                     current device (bytes from helm_peer_exchange_bytes).
+ * helm_ipc_get_handle writes the buffer's CUDA IPC handle
+ *                     (helm_ipc_handle_bytes() bytes) for the other ranks.
+ * helm_ipc_open       maps another rank's buffer from its handle.
+ * helm_ipc_close / helm_ipc_free   undo open / alloc.
+ * helm_ipc_zero       re-zeroes a buffer (after a timeout, on every rank).
+ *
+ * helm_seq_exchange_merge: bufs[world] are every rank's exchange buffer as
+ * mapped in this process (own buffer at bufs[rank]).  Stores this rank's
+ * partial state (o_part fp32 [rows, head_dim], 8-byte aligned; lse_part fp32
+ * [rows]) into slot `rank` of every buffer through NVLink, each value paired
+ * with the step's epoch in one 8-byte word, polls (at most timeout_ns) its own
+ * buffer until every rank's words of the step have arrived and merges:
+ *     M = max_r lse_r,  out = sum_r e^(lse_r - M) o_r / sum_r e^(lse_r - M)
+ * out [rows, head_dim] in out_dtype; lse_out optional fp32 [rows].  Every rank
+ * must make the same sequence of calls with the same rows and head_dim.  A
+ * wait that runs out sets HELM_DEV_TIMEOUT (helm_get_device_status); all
+ * ranks must then helm_ipc_zero their buffers before the next call.
+ * world <= 8, head_dim % 4 == 0.
+ *
+ * No counterpart in the reference (single GPU); this replaces an all-gather
+ * of the packed states followed by helm_merge_attention_states.
+ */
+int64_t helm_peer_exchange_bytes(int64_t rows, int head_dim, int world);
+int helm_ipc_alloc(int64_t bytes, void** ptr_out);
+int helm_ipc_free(void* ptr);
+int helm_ipc_zero(void* ptr, int64_t bytes, void* stream);
+int helm_ipc_handle_bytes(void);
+int helm_ipc_get_handle(const void* ptr, void* handle_out);
+int helm_ipc_open(const void* handle, void** ptr_out);
+int helm_ipc_close(void* ptr);
+int helm_seq_exchange_merge(void* const* bufs, int rank, int world, const float* o_part,
+                            const float* lse_part, int64_t rows, int head_dim, void* out,
+                            int out_dtype, float* lse_out, uint64_t timeout_ns, void* stream);
 
 #ifdef __cplusplus
 }

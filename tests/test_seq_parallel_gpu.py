@@ -89,12 +89,38 @@ def _nccl_worker(rank, world, port, out_dir):
         remap[used.long()] = torch.arange(used.numel())
         local_pool = pool[used.long()].to(dev)
         local_pt = remap[sub.long()].to(torch.int32).to(dev)
-        sp = SeqSplitAttention()
-        out, lse = sp.decode(q.to(dev), local_pool, local_pt, lens.to(dev), num_kv_heads=Hkv,
-                             page_size=P, scale=D ** -0.5)
+        kw = dict(num_kv_heads=Hkv, page_size=P, scale=D ** -0.5)
+        qs = [q] + [torch.randn(q.shape, generator=torch.Generator().manual_seed(50 + i))
+                    .to(torch.bfloat16) for i in range(3)]
+        nccl = SeqSplitAttention(exchange="nccl")
+        p2p = SeqSplitAttention(exchange="p2p")
+        res = {}
+        for i, qi in enumerate(qs):          # eager: both exchanges, repeated calls
+            for name, sp in (("nccl", nccl), ("p2p", p2p)):
+                out, lse = sp.decode(qi.to(dev), local_pool, local_pt, lens.to(dev), **kw)
+                res[f"{name}_out{i}"], res[f"{name}_lse{i}"] = out.float().cpu(), lse.cpu()
+        # the p2p step captured in a CUDA graph and replayed with new queries
+        q_static = qs[0].to(dev).clone()
+        lens_d = lens.to(dev)
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            p2p.decode(q_static, local_pool, local_pt, lens_d, **kw)
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            with torch.cuda.graph(graph, stream=side):
+                g_out, g_lse = p2p.decode(q_static, local_pool, local_pt, lens_d, **kw)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        for i, qi in enumerate(qs):
+            q_static.copy_(qi.to(dev))
+            graph.replay()
+            res[f"graph_out{i}"], res[f"graph_lse{i}"] = g_out.float().cpu(), g_lse.cpu()
         torch.cuda.synchronize()
-        np.save(os.path.join(out_dir, f"out{rank}.npy"), out.float().cpu().numpy())
-        np.save(os.path.join(out_dir, f"lse{rank}.npy"), lse.cpu().numpy())
+        assert _capi.device_status(dev) == 0
+        del graph
+        p2p.close()
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **{k: v.numpy() for k, v in res.items()})
     finally:
         dist.destroy_process_group()
 
@@ -111,14 +137,23 @@ def test_nccl_ranks_equal_single_gpu(tmp_path):
     dev = torch.device("cuda:0")
     B, Hq, Hkv, D, P, T = 1, 40, 8, 128, 16, 16384
     q, pool, pt = _problem(B, Hq, Hkv, D, P, T)
-    lse_ref = torch.empty(B, Hq, device=dev)
-    ref, _ = _capi.paged_decode_attention(q.to(dev), pool.to(dev), pt.to(dev),
-                                          torch.full((B,), T, dtype=torch.int32, device=dev),
-                                          num_kv_heads=Hkv, page_size=P, scale=D ** -0.5,
-                                          lse=lse_ref)
-    want = ref.float().cpu().numpy()
+    qs = [q] + [torch.randn(q.shape, generator=torch.Generator().manual_seed(50 + i))
+                .to(torch.bfloat16) for i in range(3)]
+    refs = []
+    for qi in qs:
+        lse_ref = torch.empty(B, Hq, device=dev)
+        ref, _ = _capi.paged_decode_attention(qi.to(dev), pool.to(dev), pt.to(dev),
+                                              torch.full((B,), T, dtype=torch.int32, device=dev),
+                                              num_kv_heads=Hkv, page_size=P, scale=D ** -0.5,
+                                              lse=lse_ref)
+        refs.append((ref.float().cpu().numpy(), lse_ref.cpu().numpy()))
     for r in range(world):
-        got = np.load(tmp_path / f"out{r}.npy")
-        assert np.all(np.abs(got - want) <= 1e-2 + 1e-2 * np.abs(want))
-        np.testing.assert_allclose(np.load(tmp_path / f"lse{r}.npy"), lse_ref.cpu().numpy(),
-                                   atol=1e-4, rtol=1e-5)
+        got = np.load(tmp_path / f"rank{r}.npz")
+        for i, (want, want_lse) in enumerate(refs):
+            for name in ("nccl", "p2p", "graph"):
+                o = got[f"{name}_out{i}"]
+                assert np.all(np.abs(o - want) <= 1e-2 + 1e-2 * np.abs(want)), (r, i, name)
+                np.testing.assert_allclose(got[f"{name}_lse{i}"], want_lse, atol=1e-4, rtol=1e-5)
+            # both exchanges merge the same fp32 states with the same formula
+            np.testing.assert_array_equal(got[f"p2p_out{i}"], got[f"nccl_out{i}"])
+            np.testing.assert_array_equal(got[f"graph_out{i}"], got[f"p2p_out{i}"])
