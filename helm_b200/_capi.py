@@ -27,6 +27,7 @@ _TORCH_TO_HELM = {torch.float32: DTYPE_FP32, torch.float16: DTYPE_FP16,
 _P, _I, _I64, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
 _SIGNATURES = {
     "helm_version": (_I, []),
+    "helm_set_decode_overlap": (_I, [_I]),
     "helm_status_string": (ctypes.c_char_p, [_I]),
     "helm_last_cuda_error": (ctypes.c_char_p, []),
     "helm_get_device_status": (_I, [ctypes.POINTER(ctypes.c_uint), _I, _P]),
@@ -405,3 +406,25 @@ def seq_exchange_merge(bufs: list, rank: int, o_part: torch.Tensor, lse_part: to
                                            helm_dtype(out.dtype), _ptr(lse_out),
                                            int(timeout_s * 1e9), _stream_handle(dev, stream))
     _check(rc, "helm_seq_exchange_merge")
+
+
+def set_decode_overlap(enable: bool) -> bool:
+    """Decode overlap for calls made from this thread (see include/helm_b200.h);
+    returns the previous setting."""
+    return bool(lib().helm_set_decode_overlap(1 if enable else 0))
+
+
+class decode_overlap:
+    """Context manager: decode overlap on (or off) inside the block."""
+
+    def __init__(self, enable: bool = True):
+        self.enable = enable
+        self.prev = False
+
+    def __enter__(self):
+        self.prev = set_decode_overlap(self.enable)
+        return self
+
+    def __exit__(self, *exc):
+        set_decode_overlap(self.prev)
+        return False

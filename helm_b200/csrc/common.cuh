@@ -27,6 +27,7 @@ namespace helm {
 static __device__ unsigned int g_device_status = 0;
 
 // Host helpers shared by the entry points (defined in helm_b200.cu).
+bool decode_overlap_enabled();
 int num_sms_current_device();
 void set_last_cuda_error(cudaError_t e);
 

@@ -15,7 +15,10 @@ namespace helm {
 
 namespace {
 thread_local char t_last_error[256] = "";
+thread_local int t_decode_overlap = 0;
 }
+
+bool decode_overlap_enabled() { return t_decode_overlap != 0; }
 
 void set_last_cuda_error(cudaError_t e) {
   std::snprintf(t_last_error, sizeof(t_last_error), "%s: %s", cudaGetErrorName(e),
@@ -38,6 +41,12 @@ int num_sms_current_device() {
 }  // namespace helm
 
 extern "C" int helm_version(void) { return 100; }
+
+extern "C" int helm_set_decode_overlap(int enable) {
+  const int prev = helm::t_decode_overlap;
+  helm::t_decode_overlap = enable != 0 ? 1 : 0;
+  return prev;
+}
 
 extern "C" const char* helm_status_string(int status) {
   switch (status) {

@@ -101,6 +101,9 @@ struct AppendArgs {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const AppendArgs a) {
+  // a decode kernel launched with overlap may be placed now (it waits for
+  // this grid before reading the rows written here)
+  asm volatile("griddepcontrol.launch_dependents;");
   constexpr int EPL = D / 32;
   const int tok = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

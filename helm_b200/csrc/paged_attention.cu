@@ -40,7 +40,7 @@ constexpr int kTileRows = 16;
 constexpr int kMaxNCW = 8;                   // most consumer warps (= workers) per CTA
 constexpr int kStageBudget = 196608;         // bytes of tile ring per CTA
 constexpr int kMaxBatch = 2048;              // prefix table held in shared memory
-constexpr int kMinTilesPerWorker = 8;
+constexpr int kMinTilesPerWorker = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -403,147 +403,74 @@ __device__ __forceinline__ PairSpan pair_span(const DecodeArgs& a, const int* s_
   return ps;
 }
 
-// Combines K partial states of pair p into one: n_smem records in shared
-// memory (warps w0.. of this CTA), n_cta CTA partials at global slots
-// c0+k+p, and, when warp_slot >= 0, the warp partial at global slot
-// warp_slot+p.  Writes either the normalised output and LSE (final) or a CTA
-// partial at slot cta_out+p.  All consumer threads take part; global sources
-// are read with at most two dependent L2 round trips (all (m, l) at once,
-// then up to kBatch O values per element at once).
+// Combines the end states of warps w0 .. w0+nw-1 of this CTA (shared-memory
+// records m[16] | l[16] | O[16][D]), which all end in pair p, plus, when
+// warp_slot >= 0, the warp partial at global slot warp_slot + p (written by a
+// warp of this CTA before the preceding barrier).  Writes the normalised
+// output and LSE (final) or a CTA partial at slot cta_out + p.  One pass, no
+// barriers: each thread owns float4 output elements and reads the (m, l) and
+// O values of all sources of its element together.
 template <typename T, int D, int NCW>
-__device__ void merge_sources(const DecodeArgs& a, int p, const float* s_states, int w0,
-                              int n_smem, int c0, int n_cta, int warp_slot, bool final_out,
-                              int cta_out, float* s_scratch) {
+__device__ void merge_group(const DecodeArgs& a, int p, const float* s_states, int w0, int nw,
+                            int warp_slot, bool final_out, int cta_out) {
   constexpr int kConsumers = NCW * 32;
   constexpr int kRec = 32 + 16 * D;
-  constexpr int kBatch = 8;
-  const int tid = threadIdx.x;
+  constexpr int D4 = D / 4;
+  constexpr int kMaxK = NCW + 1;
   const int G = a.group;
-  const int K = n_smem + n_cta + (warp_slot >= 0 ? 1 : 0);
   const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
-  float* s_m = s_scratch;        // [K][G]  m of each source, then its weight
-  float* s_l = s_m + K * G;      // [K][G]
-  float* s_M = s_l + K * G;      // [G]
-  float* s_L = s_M + 16;         // [G]
-
-  // global float offset of source k's record (O at og + hg*D, (m,l) at mlg + 2*hg)
-  auto src_o = [&](int k) -> const float* {
-    return k < n_smem + n_cta
-               ? a.cta_o + static_cast<int64_t>(c0 + k - n_smem + p) * G * D
-               : a.part_o + static_cast<int64_t>(warp_slot + p) * G * D;
-  };
-  auto src_ml = [&](int k) -> const float* {
-    return k < n_smem + n_cta
-               ? a.cta_ml + static_cast<int64_t>(c0 + k - n_smem + p) * G * 2
-               : a.part_ml + static_cast<int64_t>(warp_slot + p) * G * 2;
-  };
-  for (int e = tid; e < K * G; e += kConsumers) {
-    const int k = e / G, hg = e - (e / G) * G;
-    float m, l;
-    if (k < n_smem) {
-      m = s_states[(w0 + k) * kRec + hg];
-      l = s_states[(w0 + k) * kRec + 16 + hg];
-    } else {
-      const float2 v = __ldcg(reinterpret_cast<const float2*>(src_ml(k) + 2 * hg));
-      m = v.x;
-      l = v.y;
+  for (int e = threadIdx.x; e < G * D4; e += kConsumers) {
+    const int hg = e / D4, d4 = e - (e / D4) * D4;
+    float mk[kMaxK], lk[kMaxK];
+    float4 ok[kMaxK];
+#pragma unroll
+    for (int k = 0; k < kMaxK; ++k) {
+      mk[k] = -INFINITY;
+      lk[k] = 0.f;
+      ok[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < nw) {
+        const float* rec = s_states + (w0 + k) * kRec;
+        mk[k] = rec[hg];
+        lk[k] = rec[16 + hg];
+        ok[k] = *reinterpret_cast<const float4*>(rec + 32 + hg * D + d4 * 4);
+      } else if (k == nw && warp_slot >= 0) {
+        const int64_t slot = static_cast<int64_t>(warp_slot + p) * G + hg;
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml + slot * 2));
+        mk[k] = ml.x;
+        lk[k] = ml.y;
+        ok[k] = __ldcg(reinterpret_cast<const float4*>(a.part_o + slot * D + d4 * 4));
+      }
     }
-    s_m[e] = m;
-    s_l[e] = l;
-  }
-  consumer_barrier(kConsumers);
-  if (tid < G) {
     float M = -INFINITY;
-    for (int k = 0; k < K; ++k) M = fmaxf(M, s_m[k * G + tid]);
+#pragma unroll
+    for (int k = 0; k < kMaxK; ++k) M = fmaxf(M, mk[k]);
     const float m_use = M == -INFINITY ? 0.f : M;
     float L = 0.f;
-    for (int k = 0; k < K; ++k) {
-      const float w = exp2f(s_m[k * G + tid] - m_use);
-      s_m[k * G + tid] = w;  // weight replaces m
-      L += s_l[k * G + tid] * w;
-    }
-    s_M[tid] = M;
-    s_L[tid] = L;
-  }
-  consumer_barrier(kConsumers);
-  // O: float4 elements (head, 4 dims); `groups` threads share an element and
-  // split its sources, each keeping kBatch loads in flight; partial sums meet
-  // in shared memory.
-  constexpr int D4 = D / 4;
-  const int E4 = G * D4;
-  const int groups = E4 >= kConsumers ? 1 : kConsumers / E4;
-  const int lanes = kConsumers / groups;  // threads per group
-  float4* s_red = reinterpret_cast<float4*>(
-      (reinterpret_cast<uintptr_t>(s_L + 16) + 15) & ~static_cast<uintptr_t>(15));
-  for (int e0 = 0; e0 < E4; e0 += lanes) {
-    const int grp = tid / lanes, e = e0 + (tid - grp * lanes);
-    const bool active = grp < groups && e < E4;
-    const int hg = active ? e / D4 : 0, d4 = active ? e - hg * D4 : 0;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (active) {
-      for (int k0 = grp * kBatch; k0 < K; k0 += groups * kBatch) {
-        float4 o[kBatch];
 #pragma unroll
-        for (int i = 0; i < kBatch; ++i) {  // issue the whole batch first
-          const int k = k0 + i;
-          o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (k < K) {
-            if (k < n_smem)
-              o[i] = *reinterpret_cast<const float4*>(s_states + (w0 + k) * kRec + 32 + hg * D +
-                                                     d4 * 4);
-            else
-              o[i] = __ldcg(reinterpret_cast<const float4*>(src_o(k) + hg * D + d4 * 4));
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < kBatch; ++i) {
-          if (k0 + i < K) {
-            const float w = s_m[(k0 + i) * G + hg];
-            acc.x += w * o[i].x;
-            acc.y += w * o[i].y;
-            acc.z += w * o[i].z;
-            acc.w += w * o[i].w;
-          }
-        }
-      }
+    for (int k = 0; k < kMaxK; ++k) {
+      const float w = exp2f(mk[k] - m_use);
+      L += lk[k] * w;
+      acc.x += w * ok[k].x;
+      acc.y += w * ok[k].y;
+      acc.z += w * ok[k].z;
+      acc.w += w * ok[k].w;
     }
-    if (groups > 1) {
-      if (active) s_red[tid] = acc;
-      consumer_barrier(kConsumers);
-      if (active && grp == 0)
-        for (int q2 = 1; q2 < groups; ++q2) {
-          const float4 r = s_red[q2 * lanes + (tid - grp * lanes)];
-          acc.x += r.x;
-          acc.y += r.y;
-          acc.z += r.z;
-          acc.w += r.w;
-        }
-    }
-    if (active && grp == 0) {
-      const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-      if (final_out) {
-        const float inv = 1.f / fmaxf(s_L[hg], 1e-12f);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) store_out<T>(a, b, h * G + hg, d4 * 4 + c, vals[c] * inv);
-      } else {
-        *reinterpret_cast<float4*>(a.cta_o + (static_cast<int64_t>(cta_out + p) * G + hg) * D +
-                                   d4 * 4) = acc;
-      }
-    }
-    if (groups > 1) consumer_barrier(kConsumers);
-  }
-  if (tid < G) {
-    const float M = s_M[tid], L = s_L[tid];
     if (final_out) {
-      if (a.lse != nullptr)
-        a.lse[static_cast<int64_t>(b) * a.hq + h * G + tid] =
+      const float inv = 1.f / fmaxf(L, 1e-12f);
+      store_out<T>(a, b, h * G + hg, d4 * 4 + 0, acc.x * inv);
+      store_out<T>(a, b, h * G + hg, d4 * 4 + 1, acc.y * inv);
+      store_out<T>(a, b, h * G + hg, d4 * 4 + 2, acc.z * inv);
+      store_out<T>(a, b, h * G + hg, d4 * 4 + 3, acc.w * inv);
+      if (d4 == 0 && a.lse != nullptr)
+        a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg] =
             (M == -INFINITY || L <= 0.f) ? -INFINITY : M * kLn2 + logf(L);
     } else {
-      *reinterpret_cast<float2*>(a.cta_ml + (static_cast<int64_t>(cta_out + p) * G + tid) * 2) =
-          make_float2(M, L);
+      const int64_t slot = static_cast<int64_t>(cta_out + p) * G + hg;
+      *reinterpret_cast<float4*>(a.cta_o + slot * D + d4 * 4) = acc;
+      if (d4 == 0) *reinterpret_cast<float2*>(a.cta_ml + slot * 2) = make_float2(M, L);
     }
   }
-  consumer_barrier(kConsumers);
 }
 
 template <int D>
@@ -591,10 +518,21 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   // the merge kernel may be placed now; it waits for this grid to complete
   asm volatile("griddepcontrol.launch_dependents;");
 
+  // Launched as a programmatic dependent (decode overlap), this grid may run
+  // before the previous kernel on the stream has finished: up to here it read
+  // only the lengths; the page table is read next, and every thread waits
+  // (griddepcontrol.wait) before it reads q or the pool or writes anything.
+  // Launched normally, the waits return at once.
+
   // Pairs without tokens: zero output, LSE = -inf.
+  bool waited = false;
   for (int p = blockIdx.x; p < a.batch * a.hkv; p += gridDim.x) {
     const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
     if (s_cum[b + 1] != s_cum[b]) continue;
+    if (!waited) {
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      waited = true;
+    }
     for (int e = threadIdx.x; e < a.group * D; e += blockDim.x)
       store_out<T>(a, b, h * a.group + e / D, e % D, 0.f);
     if (a.lse != nullptr && threadIdx.x < a.group)
@@ -636,6 +574,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     int row_cur, row_nxt;
     bool ok_cur, ok_nxt;
     rows_of(j, row_cur, ok_cur);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int win = 0; win * kWin < n_stages; ++win) {
       rows_of((win + 1) * kWin + j, row_nxt, ok_nxt);  // next window's page-table reads
       for (int jj = 0; jj < kWin; ++jj) {
@@ -668,6 +607,7 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   }
 
   // ================================= consumers ================================
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int v = v0 + warp;
   const int first = v * W;
   const int my_len = max(0, min(W, total - first));
@@ -719,7 +659,6 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   // 3. pairs split across CTAs are merged by merge_split_pairs_kernel.
   constexpr int kRec = 32 + 16 * D;
   float* s_states = reinterpret_cast<float*>(smem);
-  float* s_scratch = s_states + NCW * kRec;
   __shared__ int s_endpair[NCW];
   int end_pair = -1;
   if (!ok) {
@@ -745,12 +684,11 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     if (p >= 0) {
       const PairSpan ps = pair_span(a, s_cum, W, total, p);
       const int cf = ps.vf / NCW, cl = ps.vl / NCW;
-      if (cf == cl) {  // the whole pair is in this CTA
-        merge_sources<T, D, NCW>(a, p, s_states, w0, w1 - w0, 0, 0,
-                                 ps.last_continues ? ps.vl : -1, true, 0, s_scratch);
-      } else {
-        merge_sources<T, D, NCW>(a, p, s_states, w0, w1 - w0, 0, 0, -1, false, cta, s_scratch);
-      }
+      if (cf == cl)  // the whole pair is in this CTA
+        merge_group<T, D, NCW>(a, p, s_states, w0, w1 - w0, ps.last_continues ? ps.vl : -1,
+                               true, 0);
+      else
+        merge_group<T, D, NCW>(a, p, s_states, w0, w1 - w0, -1, false, cta);
     }
     w0 = w1;
   }
@@ -770,6 +708,7 @@ constexpr int kMergeBatch = 16;
 template <typename T, int D, int NCW>
 __global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const DecodeArgs a) {
   extern __shared__ int s_cum_m[];
+  asm volatile("griddepcontrol.launch_dependents;");
   const int p = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp == 0) build_prefix(a, s_cum_m, lane);
@@ -893,9 +832,20 @@ int launch(const DecodeArgs& a, const void* pool, int64_t pool_rows, int grid,
     return HELM_ERR_CUDA;
   DecodeArgs args = a;
   args.num_workers = grid * L::NCW;
-  paged_decode_kernel<T, D, NT>
-      <<<grid, L::kThreads, L::smem_bytes(a.batch), stream>>>(map, args);
-  if (cudaGetLastError() != cudaSuccess) return HELM_ERR_CUDA;
+  {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(L::kThreads);
+    cfg.dynamicSmemBytes = L::smem_bytes(a.batch);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = decode_overlap_enabled() ? 1 : 0;
+    if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<T, D, NT>, map, args) != cudaSuccess)
+      return HELM_ERR_CUDA;
+  }
   // merge of split pairs: a programmatic dependent of the decode kernel
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.hkv),

@@ -91,6 +91,7 @@ __device__ __forceinline__ uint2* slot_ptr(unsigned char* buf, int64_t stride, i
 }
 
 __global__ void __launch_bounds__(128) seq_exchange_merge_kernel(PeerExchangeArgs a) {
+  asm volatile("griddepcontrol.launch_dependents;");
   const int c = blockIdx.x;
   const int D = a.head_dim;
   const int64_t r0 = (int64_t)c * a.chunk_rows;

@@ -274,7 +274,9 @@ class GraphDecoder:
         saved = (self.ids.clone(), self.pos.clone())
         self.mgr.kvcms[0]._graph = self.ctx
         try:
-            with torch.cuda.graph(g, stream=side):
+            # decode overlap: inside the step the kernel before each attention
+            # is the fused append, which writes no page table or length
+            with torch.cuda.graph(g, stream=side), _capi.decode_overlap():
                 self._step_body()
         finally:
             self.mgr.kvcms[0]._graph = None
@@ -351,6 +353,7 @@ class GraphDecoder:
         """The captured body run once without capture (same bookkeeping)."""
         self.mgr.kvcms[0]._graph = self.ctx
         try:
-            self._step_body()
+            with _capi.decode_overlap():
+                self._step_body()
         finally:
             self.mgr.kvcms[0]._graph = None

@@ -230,3 +230,61 @@ def test_invalid_arguments_raise():
         pool2 = torch.randn(8, 2, 2, 16, 96, dtype=torch.bfloat16, device=dev)
         _capi.paged_decode_attention(q2, pool2, pt.to(dev), kl.to(dev), num_kv_heads=2,
                                      page_size=16, scale=0.1)
+
+
+def _append_then_decode(steps, overlap, graph):
+    """Per step: the fused append writes q_out and one K/V row per sequence,
+    then decode attention reads both.  Returns the outputs of every step."""
+    from helm_b200 import _capi
+    dev = torch.device("cuda:0")
+    B, Hq, Hkv, D, P, T0 = 2, 8, 2, 128, 16, 100
+    g = torch.Generator().manual_seed(11)
+    npg = (T0 + steps) // P + 1
+    pool = torch.randn(B * npg, 2, Hkv, P, D, generator=g).to(torch.bfloat16).to(dev)
+    pt = torch.arange(B * npg, dtype=torch.int32).view(B, npg).to(dev)
+    qs = torch.randn(steps, B, Hq, D, generator=g).to(torch.bfloat16).to(dev)
+    ks = torch.randn(steps, B, Hkv, D, generator=g).to(torch.bfloat16).to(dev)
+    vs = torch.randn(steps, B, Hkv, D, generator=g).to(torch.bfloat16).to(dev)
+    cos = torch.rand(steps, B, D, generator=g).to(torch.bfloat16).to(dev)
+    sin = torch.rand(steps, B, D, generator=g).to(torch.bfloat16).to(dev)
+    rows = torch.stack([(pt[:, (T0 + s) // P].long() * P + (T0 + s) % P) for s in range(steps)])
+    lens = torch.stack([torch.full((B,), T0 + s + 1, dtype=torch.int32, device=dev)
+                        for s in range(steps)])
+    q_out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=dev)
+    outs = torch.empty(steps, B, Hq, D, dtype=torch.bfloat16, device=dev)
+
+    def run():
+        for s in range(steps):
+            _capi.kv_append(q=qs[s], k=ks[s], v=vs[s], q_out=q_out, cos=cos[s], sin=sin[s],
+                            pool=pool, slot_rows=rows[s], page_size=P)
+            _capi.paged_decode_attention(q_out, pool, pt, lens[s], num_kv_heads=Hkv, page_size=P,
+                                         scale=D ** -0.5, out=outs[s], max_kv_len_hint=T0 + steps)
+
+    with _capi.decode_overlap(overlap):
+        if graph:
+            run()        # warm-up outside capture (workspace), then reset the pool rows
+            torch.cuda.synchronize()
+            cg = torch.cuda.CUDAGraph()
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                with torch.cuda.graph(cg, stream=side):
+                    run()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            cg.replay()
+        else:
+            run()
+    torch.cuda.synchronize()
+    assert _capi.device_status(dev) == 0
+    return outs.cpu()
+
+
+def test_decode_overlap_sees_the_preceding_append():
+    """Decode overlap places the decode kernel while the fused append that
+    writes its query and newest K/V rows still runs; the results must equal
+    those of plain stream order, bit for bit, eager and inside a CUDA graph."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    ref = _append_then_decode(6, overlap=False, graph=False)
+    assert torch.equal(_append_then_decode(6, overlap=True, graph=False), ref)
+    assert torch.equal(_append_then_decode(6, overlap=True, graph=True), ref)
