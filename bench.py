@@ -472,7 +472,7 @@ def run_model(args, rank: int, world: int, dev: torch.device):
         wm = int((1 - w["cold"]) * S * tok_bytes * L)
     kcfg = KVOffloadConfig.from_model(model, page_size=w["page"], gpu_watermark_bytes=wm)
     mgr = KVOffloadManager(model, kcfg)
-    gd = GraphDecoder(model, mgr, max_len=S + K + 1)
+    gd = GraphDecoder(model, mgr, max_len=S + K + 1, fused=args.stage == "fused")
     try:
         for _ in range(max(args.warmup, 3)):
             gd.generate(prompt.to(dev, non_blocking=True), 4)
@@ -522,6 +522,10 @@ def run_model(args, rank: int, world: int, dev: torch.device):
                                    f"{int(w['cold'] * 100)}% of prompt pages host-resident",
                        "execution": "one CUDA graph replay per decode step (re-captured when "
                                     "the cold page set changes)",
+                       "stage": ("FusedDecodeStage: 7 launches per layer (fused RMSNorm/SwiGLU/"
+                                 "residual GEMVs, fused append, paged attention)"
+                                 if args.stage == "fused" else
+                                 "HF modules with the patched attention forward"),
                        "l2": "weights + KV per step exceed L2",
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -538,8 +542,10 @@ def run_model(args, rank: int, world: int, dev: torch.device):
                             "prefill and graph captures included"},
             "host_plan_ms_per_step": plan_ms, "graph_captures": captures,
             "paging": stats,
-            # this library's kernels per step: fused append + paged attention per layer
-            "gpu_launches": 2 * L * K, "clocks": clocks.summary()}
+            # this library's kernels per step: per layer append + attention (+ merge) and,
+            # with the fused stage, four GEMVs; plus the lm_head GEMV
+            "gpu_launches": (7 * L + 1 if args.stage == "fused" else 3 * L) * K,
+            "clocks": clocks.summary()}
     print(json.dumps(line), flush=True)
 
 
@@ -554,6 +560,8 @@ def main():
                     help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
                          "configs[3] split across the GPUs (strong scaling); or whole-model "
                          "decode tok/s of configs[0] (config1) / configs[2] (config3)")
+    ap.add_argument("--stage", choices=["fused", "hf"], default="fused",
+                    help="config1/config3: decode step as FusedDecodeStage or as HF modules")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="seqsplit128k: how partial states cross GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -56,6 +56,11 @@ _SIGNATURES = {
     "helm_copy_pages": (_I, [_P, _P, _I64, _P, _P, _I64, _P]),
     "helm_gather_kv": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
     "helm_merge_attention_states": (_I, [_P, _I, _I64, _P, _I64, _I, _I64, _I, _P, _I, _P, _P]),
+    "helm_decode_gemv": (_I, [_P, _I64, _P, _F, _P, _P, _I64, _I64, _P, _I64, _P, _I64, _I, _I,
+                              _I, _P]),
+    "helm_decode_gemv_allreduce": (_I, [_P, _I, _I, _P, _I64, _P, _I64, _I64, _P, _I64, _P,
+                                        _I64, _I, _I, ctypes.c_uint64, _P]),
+    "helm_decode_gemv_allreduce_bytes": (_I64, [_I64, _I, _I]),
     "helm_peer_exchange_bytes": (_I64, [_I64, _I, _I]),
     "helm_ipc_alloc": (_I, [_I64, ctypes.POINTER(_P)]),
     "helm_ipc_free": (_I, [_P]),
@@ -428,3 +433,61 @@ class decode_overlap:
     def __exit__(self, *exc):
         set_decode_overlap(self.prev)
         return False
+
+
+def decode_gemv(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor,
+                norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                w2: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+                stream=None) -> torch.Tensor:
+    """out[b] = W . f(x[b]) with the fused RMSNorm / SwiGLU / residual of
+    helm_decode_gemv.  x [B, K] (unit inner stride), w (and w2) [N, K]
+    contiguous, out [B, N] (model dtype or fp32), residual [B, N] or None."""
+    B, K = x.shape
+    N = w.shape[0]
+    if x.stride(1) != 1 or not w.is_contiguous() or (w2 is not None and not w2.is_contiguous()):
+        raise HelmError("decode_gemv: x needs a unit inner stride, weights must be contiguous")
+    if w.shape[1] != K or out.shape[0] != B or out.shape[1] != N or out.stride(1) != 1:
+        raise HelmError("decode_gemv: shape mismatch")
+    if residual is not None and (residual.shape != out.shape or residual.stride(1) != 1):
+        raise HelmError("decode_gemv: residual must match out")
+    dev = x.device
+    with torch.cuda.device(dev):
+        rc = lib().helm_decode_gemv(
+            x.data_ptr(), x.stride(0), _ptr(norm_w), float(eps), w.data_ptr(), _ptr(w2), N, K,
+            _ptr(residual), residual.stride(0) if residual is not None else 0,
+            out.data_ptr(), out.stride(0), 1 if out.dtype == torch.float32 else 0, B,
+            helm_dtype(x.dtype), _stream_handle(dev, stream))
+    _check(rc, "helm_decode_gemv")
+    return out
+
+
+def decode_gemv_allreduce_bytes(n: int, batch: int, world: int) -> int:
+    v = lib().helm_decode_gemv_allreduce_bytes(n, batch, world)
+    if v < 0:
+        raise HelmError("unsupported all-reduce geometry")
+    return int(v)
+
+
+def decode_gemv_allreduce(bufs: list, rank: int, x: torch.Tensor, w: torch.Tensor, *,
+                          out: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                          timeout_s: float = 5.0, stream=None) -> torch.Tensor:
+    """Row-parallel projection with its all-reduce: out[b] = residual[b] +
+    sum over ranks of W_r x_r[b] (this rank's W_r [N, K_r], x_r [B, K_r]).
+    bufs: every rank's exchange buffer mapped here (decode_gemv_allreduce_bytes)."""
+    B, K = x.shape
+    N = w.shape[0]
+    if x.stride(1) != 1 or not w.is_contiguous() or w.shape[1] != K:
+        raise HelmError("decode_gemv_allreduce: x [B, K] unit inner stride, w [N, K] contiguous")
+    if out.shape != (B, N) or out.stride(1) != 1 or out.dtype != x.dtype:
+        raise HelmError("decode_gemv_allreduce: out must be [B, N] in the model dtype")
+    if residual is not None and (residual.shape != out.shape or residual.stride(1) != 1):
+        raise HelmError("decode_gemv_allreduce: residual must match out")
+    dev = x.device
+    arr = (ctypes.c_void_p * len(bufs))(*bufs)
+    with torch.cuda.device(dev):
+        rc = lib().helm_decode_gemv_allreduce(
+            arr, rank, len(bufs), x.data_ptr(), x.stride(0), w.data_ptr(), N, K, _ptr(residual),
+            residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), B,
+            helm_dtype(x.dtype), int(timeout_s * 1e9), _stream_handle(dev, stream))
+    _check(rc, "helm_decode_gemv_allreduce")
+    return out

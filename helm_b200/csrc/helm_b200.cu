@@ -10,6 +10,7 @@
 #include "paged_attention.cu"
 #include "paged_attention_noalloc.cu"
 #include "peer_exchange.cu"
+#include "decode_gemv.cu"
 
 namespace helm {
 

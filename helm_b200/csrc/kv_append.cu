@@ -101,9 +101,12 @@ struct AppendArgs {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const AppendArgs a) {
-  // a decode kernel launched with overlap may be placed now (it waits for
-  // this grid before reading the rows written here)
+  // Programmatic dependent launch both ways: a decode kernel launched with
+  // overlap may be placed now (it waits for this grid before reading the rows
+  // written here), and this grid waits for the kernel before it (which
+  // writes q / k / v) before reading anything.
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   constexpr int EPL = D / 32;
   const int tok = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -122,10 +125,12 @@ __global__ void __launch_bounds__(kAppendWarps * 32) kv_append_kernel(const Appe
   const int64_t head_elems = static_cast<int64_t>(a.page_size) * D;
   T* pool = static_cast<T*>(a.pool);
   const int rows_total = a.hq + 2 * a.hkv;
-  for (int hr = warp; hr < rows_total; hr += kAppendWarps) {
+  // one head row per warp: grid.y covers the token's q, k and v rows
+  const int hr = blockIdx.y * kAppendWarps + warp;
+  if (hr < rows_total) {
     float x[EPL];
     if (hr < a.hq) {
-      if (a.q_out == nullptr) continue;
+      if (a.q_out == nullptr) return;
       load_row<T, EPL>(static_cast<const T*>(a.q) + tok * a.q_st + hr * a.q_sh + lane * EPL, x);
       norm_rope<T, D>(x, static_cast<const T*>(a.qw), a.eps, cosp, sinp, lane);
       store_row<T, EPL>(static_cast<T*>(a.q_out) + tok * a.qo_st + hr * a.qo_sh + lane * EPL, x);
@@ -178,20 +183,30 @@ __global__ void kv_scatter_rows_kernel(const AppendArgs a, int head_dim) {
 
 template <typename T>
 int launch_append(int head_dim, const AppendArgs& a, int n, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n, (a.hq + 2 * a.hkv + kAppendWarps - 1) / kAppendWarps);
+  cfg.blockDim = dim3(kAppendWarps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   switch (head_dim) {
     case 64:
-      kv_append_kernel<T, 64><<<n, kAppendWarps * 32, 0, s>>>(a);
+      e = cudaLaunchKernelEx(&cfg, kv_append_kernel<T, 64>, a);
       break;
     case 128:
-      kv_append_kernel<T, 128><<<n, kAppendWarps * 32, 0, s>>>(a);
+      e = cudaLaunchKernelEx(&cfg, kv_append_kernel<T, 128>, a);
       break;
     case 256:
-      kv_append_kernel<T, 256><<<n, kAppendWarps * 32, 0, s>>>(a);
+      e = cudaLaunchKernelEx(&cfg, kv_append_kernel<T, 256>, a);
       break;
     default:
       return HELM_ERR_UNSUPPORTED;
   }
-  return cudaGetLastError() == cudaSuccess ? HELM_OK : HELM_ERR_CUDA;
+  return e == cudaSuccess ? HELM_OK : HELM_ERR_CUDA;
 }
 
 }  // namespace

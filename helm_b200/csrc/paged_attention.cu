@@ -540,11 +540,15 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
   }
 
   const int total = s_cum[a.batch] * a.hkv;
-  if (total == 0) return;
-  const int W = div_up(total, a.num_workers);
+  const int W = total > 0 ? div_up(total, a.num_workers) : 0;
   const int v0 = blockIdx.x * NCW;
-  const int n_stages = max(0, min(W, total - v0 * W));
-  if (n_stages == 0) return;
+  const int n_stages = total > 0 ? max(0, min(W, total - v0 * W)) : 0;
+  if (n_stages == 0) {
+    // nothing to stream; still wait, so that this grid cannot complete before
+    // the kernel it depends on (later kernels rely on that ordering)
+    if (!waited) asm volatile("griddepcontrol.wait;" ::: "memory");
+    return;
+  }
 
   if (warp == NCW) {
     // ================================ producer ================================
@@ -713,6 +717,9 @@ __global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (warp == 0) build_prefix(a, s_cum_m, lane);
   __syncthreads();
+  // every thread waits for the decode kernel (complete and visible), also the
+  // ones with nothing to merge: this grid must not complete before it
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int total = s_cum_m[a.batch] * a.hkv;
   if (total == 0) return;
   const int W = div_up(total, a.num_workers);
@@ -726,8 +733,6 @@ __global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const 
   const int e = blockIdx.y * kMergeThreads + threadIdx.x;
   if (e >= G * D4) return;
   const int hg = e / D4, d4 = e - (e / D4) * D4;
-  // the decode kernel's partials are complete and visible after this
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   float M = -INFINITY, Lsum = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k0 = 0; k0 < K; k0 += kMergeBatch) {

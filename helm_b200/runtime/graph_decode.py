@@ -172,7 +172,10 @@ class GraphDecoder:
     """Greedy generation with graph-replayed decode steps (batch of equal-length
     prompts, dense page lists).  Produces the same tokens as DecodeLoop."""
 
-    def __init__(self, model, kv_offload_mgr, max_len: int):
+    def __init__(self, model, kv_offload_mgr, max_len: int, fused: bool = False,
+                 max_batch: int = 16):
+        """fused: run the decode step as FusedDecodeStage (seven launches per
+        layer) instead of the HF modules with the patched attention."""
         self.model = model
         self.mgr = kv_offload_mgr
         self.max_len = max_len
@@ -186,6 +189,10 @@ class GraphDecoder:
         self.ctx: Optional[_GraphContext] = None
         self.cold_sig = None
         self.captures = 0
+        self.stage = None
+        if fused:
+            from .decode_stage import FusedDecodeStage
+            self.stage = FusedDecodeStage(model, max_batch)
         self.h2d_bytes = 0
 
     # -- host side of a step ------------------------------------------------------
@@ -258,9 +265,12 @@ class GraphDecoder:
     def _step_body(self) -> None:
         ctx = self.ctx
         ctx.begin_step()
-        out = self.model(input_ids=self.ids, attention_mask=ctx.mask4d, position_ids=self.pos,
-                         use_cache=False, logits_to_keep=1)
-        self.logits.copy_(out.logits[:, -1, :])
+        if self.stage is not None:
+            self.stage.step(self.ids, self.pos, self.logits, ctx)
+        else:
+            out = self.model(input_ids=self.ids, attention_mask=ctx.mask4d, position_ids=self.pos,
+                             use_cache=False, logits_to_keep=1)
+            self.logits.copy_(out.logits[:, -1, :])
         self.ids.copy_(torch.argmax(self.logits, dim=-1, keepdim=True))
         self.pos.add_(1)
         ctx.end_step()
@@ -291,7 +301,10 @@ class GraphDecoder:
 
     @torch.no_grad()
     def generate(self, input_ids, max_new_tokens: int, keep_logits: bool = False,
-                 reserve_pages: bool = True):
+                 reserve_pages: bool = True, forced_tokens=None):
+        """Greedy tokens [B, n] (and, with keep_logits, each step's logits).
+        forced_tokens [B, >= n-1] (teacher forcing): step s+1 is fed
+        forced_tokens[:, s] instead of the argmax, which is still returned."""
         from .decode_loop import DecodeLoop
         B, S = input_ids.shape
         if S + max_new_tokens > self.max_len:
@@ -315,6 +328,9 @@ class GraphDecoder:
         self.logits = torch.empty_like(logits0)
         history = torch.empty(B, max_new_tokens, dtype=torch.long, device=self.dev)
         history[:, 0] = self.ids[:, 0]
+        if forced_tokens is not None:
+            forced_tokens = forced_tokens.to(self.dev)
+            self.ids.copy_(forced_tokens[:, 0:1])
         all_logits = [logits0.float()] if keep_logits else None
         # decode-phase timing (CUDA events around steps 1.., host planning time)
         self.decode_events = (torch.cuda.Event(enable_timing=True),
@@ -333,12 +349,16 @@ class GraphDecoder:
                     history[:, step] = self.ids[:, 0]
                     if keep_logits:
                         all_logits.append(self.logits.float().clone())
+                    if forced_tokens is not None and step < forced_tokens.shape[1]:
+                        self.ids.copy_(forced_tokens[:, step:step + 1])
                     continue
                 self._capture()
             self.graph.replay()
             history[:, step] = self.ids[:, 0]
             if keep_logits:
                 all_logits.append(self.logits.float().clone())
+            if forced_tokens is not None and step < forced_tokens.shape[1]:
+                self.ids.copy_(forced_tokens[:, step:step + 1])
         self.decode_events[1].record()
         out = (history, all_logits) if keep_logits else history
         self.graph = None   # captured pointers belong to this request

@@ -274,6 +274,44 @@ int helm_seq_exchange_merge(void* const* bufs, int rank, int world, const float*
                             const float* lse_part, int64_t rows, int head_dim, void* out,
                             int out_dtype, float* lse_out, uint64_t timeout_ns, void* stream);
 
+/*
+ * One matrix-vector product of a decode step with its neighbours fused in
+ * (the GPU stage around the attention call; HELM runs these as the eager HF
+ * modules of a stage, executor.py:420 / decode_tracer.py:274-336):
+ *   y[b] = W . rmsnorm(x[b])        when norm_w != NULL (eps: the norm's eps)
+ *   y[b] = silu(W x[b]) * (W2 x[b]) when w2 != NULL (SwiGLU)
+ *   y[b] = residual[b] + W x[b]     when residual != NULL
+ * (norm and SwiGLU/residual may be combined), rounding to `dtype` where HF's
+ * eager modules do.  x [batch, k] (row stride x_stride elements), W / W2
+ * [n, k] row-major 16-byte aligned, k % 8 == 0, batch <= 16, batch * k * 2
+ * bytes <= 200 KiB; y [batch, n] (row stride y_stride) in dtype, or fp32 when
+ * y_fp32.  y may alias residual.  dtype: HELM_DTYPE_BF16 or HELM_DTYPE_FP16.
+ */
+int helm_decode_gemv(const void* x, int64_t x_stride, const void* norm_w, float eps,
+                     const void* w, const void* w2, int64_t n, int64_t k, const void* residual,
+                     int64_t res_stride, void* y, int64_t y_stride, int y_fp32, int batch,
+                     int dtype, void* stream);
+
+/*
+ * Row-parallel projection of tensor-parallel decode with its all-reduce in
+ * the same kernel: y[b] = residual[b] + sum over ranks r of W_r x_r[b], where
+ * this rank holds W_r [n, k] (its slice of the input dim) and x_r [batch, k].
+ * Each CTA stores its rows' fp32 partials into every rank's buffer over
+ * NVLink as {value, epoch} words, polls its own buffer (at most timeout_ns)
+ * for the other ranks' partials of the same rows and sums them in rank order,
+ * so every rank gets the same y.  bufs[world]: every rank's exchange buffer
+ * (helm_decode_gemv_allreduce_bytes(n, max batch, world) bytes, zeroed, from
+ * helm_ipc_alloc / helm_ipc_open), one buffer per (n, batch) use.  All ranks
+ * make the same calls in the same order.  No counterpart in the reference
+ * (single GPU); replaces o_proj / down_proj + an all-reduce + the residual add.
+ */
+int helm_decode_gemv_allreduce(void* const* bufs, int rank, int world, const void* x,
+                               int64_t x_stride, const void* w, int64_t n, int64_t k,
+                               const void* residual, int64_t res_stride, void* y,
+                               int64_t y_stride, int batch, int dtype, uint64_t timeout_ns,
+                               void* stream);
+int64_t helm_decode_gemv_allreduce_bytes(int64_t n, int batch, int world);
+
 #ifdef __cplusplus
 }
 #endif
