@@ -430,6 +430,112 @@ MODEL_WORKLOADS = {
 }
 
 
+TP_WORKLOADS = {
+    # Qwen3-14B at 131072 tokens of context, B=1; KV heads and weights
+    # sharded over the GPUs (tensor parallel), decode tok/s at N = 1, 2, 4, 8
+    "config4": dict(name="qwen3-14b", dtype=torch.bfloat16, batch=1, context=131072, steps=128,
+                    arch=dict(hidden=5120, layers=40, q_heads=40, kv_heads=8, head_dim=128,
+                              intermediate=17408, vocab=151936, qk_norm=True, theta=1e6)),
+    # Llama-2-13B fp16, B=16 x 2048-token contexts, MHA heads sharded
+    "config5": dict(name="llama2-13b", dtype=torch.float16, batch=16, context=2048, steps=256,
+                    arch=dict(hidden=5120, layers=40, q_heads=40, kv_heads=40, head_dim=128,
+                              intermediate=13824, vocab=32000, qk_norm=False, theta=1e4)),
+}
+
+
+def run_tp(args, rank: int, world: int, dev: torch.device):
+    """Decode tok/s of a tensor-parallel model over `world` GPUs (BASELINE
+    configs[3] / configs[4]).  Random-init weights drawn per shard; the
+    context's K/V pages are filled with N(0,1) values (prefill is not part of
+    the decode metric and a 131072-token prefill is not timed here).  Total
+    work is fixed as N grows (strong scaling); time = max over ranks."""
+    from helm_b200 import _capi
+    from helm_b200.runtime.tp_decode import TPDecodeModel, synthetic_shard
+    w = TP_WORKLOADS[args.workload]
+    K = args.steps if args.steps_given else w["steps"]
+    W = max(args.warmup, 3)
+    Bq, ctx, arch = w["batch"], w["context"], w["arch"]
+    e2e_steps = min(K, 32)
+    shard = synthetic_shard(arch, rank, world, w["dtype"], dev)
+    tp = TPDecodeModel(shard, batch=Bq, max_len=ctx + 3 + W + K + e2e_steps + 16, page_size=16)
+    try:
+        tp.fill_kv(ctx)
+        for _ in range(3):
+            tp.step()
+        tp.capture()
+        for _ in range(W):
+            tp.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        stream = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index) as clocks:
+            e0.record(stream)
+            for _ in range(K):
+                tp.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        ms_rank = e0.elapsed_time(e1) / K
+        # end to end: every step's tokens read back to pinned host memory (streaming)
+        host_tok = torch.empty(Bq, 1, dtype=torch.long).pin_memory()
+        if world > 1:
+            torch.distributed.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            tp.replay()
+            host_tok.copy_(tp.ids, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+        t = torch.tensor([ms_rank, e2e_ms], dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+        status = _capi.device_status(dev)
+        # bytes this rank reads per step: its weight shard + its KV heads at the mean context
+        wbytes = sum(x.numel() for lw in shard.layers for x in
+                     (lw.wqkv, lw.wo, lw.wg, lw.wu, lw.wd)) * shard.embed.element_size()
+        wbytes += shard.lm_head.numel() * shard.lm_head.element_size() + Bq * arch["hidden"] * 2
+        mean_ctx = ctx + 3 + W + K / 2
+        kv_bytes = len(shard.layers) * Bq * mean_ctx * 2 * shard.hkv * shard.head_dim * 2
+    finally:
+        tp.close()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+    if rank != 0:
+        return
+    hbm, peak_src = _peaks()
+    step_bytes = wbytes + kv_bytes
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    line = {"metric": METRIC, "value": Bq / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if w["dtype"] == torch.bfloat16 else "fp16",
+            "data": "synthetic (random-init weight shards, N(0,1) K/V context)",
+            "config": {"workload": f"{args.workload}: {w['name']} random-init, batch {Bq}, "
+                                   f"{ctx}-token context (K/V filled synthetically), greedy "
+                                   f"decode, 16-token pages, tensor parallel x{world} (KV heads, "
+                                   f"q/k/v/gate/up rows, o/down columns, lm_head vocab)",
+                       "execution": "one CUDA graph replay per step; row-parallel projections "
+                                    "all-reduce over NVLink inside the GEMV kernel; greedy pick "
+                                    "by one NCCL all-gather",
+                       "l2": "weights + K/V per step exceed L2",
+                       "parallelism": f"tp{world}"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "bytes_per_step_per_gpu": step_bytes, "weight_bytes_per_gpu": wbytes,
+                         "kv_bytes_per_step_per_gpu": kv_bytes,
+                         "roofline_tok_s": Bq / (step_bytes / (hbm * 1e9)),
+                         "peak_source": peak_src},
+            "e2e": {"value": Bq / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": Bq * 8,
+                    "note": "graph replay + per-step copy of the new tokens to pinned host "
+                            "memory and a host sync (token streaming)"},
+            "gpu_launches": (7 * len(shard.layers) + 1) * K,
+            "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def _h2d_gbs(dev: torch.device, nbytes: int = 1 << 30) -> float:
     """Pinned host -> device copy bandwidth (best of 5), the link roofline."""
     h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
@@ -555,7 +661,8 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["config2", "seqsplit128k"] + sorted(MODEL_WORKLOADS),
+    ap.add_argument("--workload", choices=["config2", "seqsplit128k"] + sorted(MODEL_WORKLOADS)
+                    + sorted(TP_WORKLOADS),
                     default="config2",
                     help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
                          "configs[3] split across the GPUs (strong scaling); or whole-model "
@@ -591,6 +698,8 @@ def main():
             run_seqsplit(args, rank, world, dev)
         elif args.workload in MODEL_WORKLOADS:
             run_model(args, rank, world, dev)
+        elif args.workload in TP_WORKLOADS:
+            run_tp(args, rank, world, dev)
         else:
             run_b200(args, rank, world, dev)
     finally:

@@ -491,3 +491,16 @@ def decode_gemv_allreduce(bufs: list, rank: int, x: torch.Tensor, w: torch.Tenso
             helm_dtype(x.dtype), int(timeout_s * 1e9), _stream_handle(dev, stream))
     _check(rc, "helm_decode_gemv_allreduce")
     return out
+
+
+def gemv_max_batch(k: int, elem: int = 2) -> int:
+    """Largest batch (<= 16) helm_decode_gemv stages for input width k: x of
+    every batch row plus the weight-stream ring must fit in shared memory."""
+    for nb in (16, 8, 4, 2, 1):
+        threads = 512 if nb == 1 else 256
+        ring = 128 if nb >= 8 else 256
+        stride = k if nb == 1 else k + 8
+        static = 4 * (threads // 32) * 16 * nb * 2 + 1024
+        if (nb * stride * elem + 127) // 128 * 128 + threads * ring + static <= 224 * 1024:
+            return nb
+    raise HelmError(f"input width {k} too large for decode_gemv")

@@ -29,14 +29,28 @@
 namespace helm {
 namespace {
 
-constexpr int kGemvUnroll = 4;
+constexpr int kGemvMaxSmem = 224 * 1024;  // x of all batch rows, staged per CTA
 // threads per CTA: fewer for wide batches so that the accumulators fit
 template <int NB>
 struct GemvShape {
   static constexpr int kThreads = NB == 1 ? 512 : 256;
   static constexpr int kWarps = kThreads / 32;
-  static constexpr int kMinBlocks = NB <= 4 ? 2 : 1;  // at least two CTAs per SM when narrow
+  // bytes of weight stream in flight per lane (cp.async ring): 128 KB per CTA
+  // for one batch row (512 threads), 64 KB for 2-4 rows, 32 KB where x of 8-16
+  // rows takes the shared memory
+  static constexpr int kRingPerLane = NB >= 8 ? 128 : 256;
 };
+
+template <int NB>
+__host__ __device__ __forceinline__ int64_t gemv_x_stride(int64_t k) {
+  return NB == 1 ? k : k + 8;  // rows of x in smem start 4 banks apart
+}
+
+template <typename T, int NB>
+size_t gemv_smem_bytes(int64_t k) {
+  return (static_cast<size_t>(NB) * gemv_x_stride<NB>(k) * sizeof(T) + 127) / 128 * 128 +
+         static_cast<size_t>(GemvShape<NB>::kThreads) * GemvShape<NB>::kRingPerLane;
+}
 
 constexpr int kArMaxRanks = 8;
 constexpr int64_t kArHeaderBytes = 8192;  // uint32 epoch per CTA (<= 2048 CTAs)
@@ -58,15 +72,8 @@ struct GemvArgs {
   int64_t y_stride;
   int y_fp32;
   int batch;
+  int ksplit;
 };
-
-__device__ __forceinline__ uint4 ld_stream_v4(const void* p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
 
 template <typename T>
 __device__ __forceinline__ float2 unpack2(uint32_t v);
@@ -158,39 +165,95 @@ __device__ __forceinline__ bool allreduce_value(const GemvArgs& a, uint32_t e, i
   return true;
 }
 
-template <typename T, int NB, bool AR>
-__global__ void __launch_bounds__(GemvShape<NB>::kThreads, AR ? 1 : GemvShape<NB>::kMinBlocks) decode_gemv_kernel(const GemvArgs a) {
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Weight stream and math.  A warp owns a block of 16 weight rows and a slice
+// of K.  Per 16-wide k-step, lane l copies (cp.async, 16 bytes) row l % 16,
+// k-half l / 16 of the block into its own slot of a shared-memory ring; that
+// slot is exactly the row address ldmatrix.x4 wants from lane l for the A
+// fragment of mma.m16n8k16 (weight rows = M, k = K, batch rows = N, x read
+// from shared memory as the B fragment).  Each lane waits only for its own
+// copies (cp.async.wait_group) before the warp-wide ldmatrix, after a
+// __syncwarp.  kDepth ring items per lane stay in flight without registers.
+template <typename T, int NB, bool AR, bool GLU>
+__global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel(const GemvArgs a) {
   constexpr int kGemvThreads = GemvShape<NB>::kThreads;
   constexpr int kGemvWarps = GemvShape<NB>::kWarps;
-  extern __shared__ __align__(16) uint8_t gemv_smem[];
-  T* xs = reinterpret_cast<T*>(gemv_smem);  // [NB][K]
+  constexpr int kStreams = GLU ? 2 : 1;
+  constexpr int kU = GLU ? 2 : 4;  // k-steps per ring item
+  constexpr int kDepth = GemvShape<NB>::kRingPerLane / (16 * kU * kStreams);
+  static_assert(kDepth >= 2, "ring needs two items");
+  constexpr int NT = NB <= 8 ? 1 : 2;  // n-tiles of 8 batch columns
+  extern __shared__ __align__(128) uint8_t gemv_smem[];
+  const int64_t K = a.k;
+  const int64_t XS = gemv_x_stride<NB>(K);  // padded: B-fragment reads avoid bank conflicts
+  T* xs = reinterpret_cast<T*>(gemv_smem);  // [NB][XS]
+  const uint32_t ring = smem_addr(gemv_smem) +
+                        static_cast<uint32_t>((NB * XS * sizeof(T) + 127) / 128 * 128);
   __shared__ float s_red[kGemvWarps];
   __shared__ float s_scale;
+  __shared__ float s_part[kGemvWarps][16][NB][kStreams];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t K = a.k;
+  const int gq = lane >> 2, tq = lane & 3;
   const T* x = static_cast<const T*>(a.x);
   const T* nw = static_cast<const T*>(a.norm_w);
   const T* W = static_cast<const T*>(a.w);
   const T* W2 = static_cast<const T*>(a.w2);
-  const bool glu = W2 != nullptr;
-  const int64_t chunks = K / 8;  // 16-byte chunks per row (K % 8 == 0)
-  // Launched as a programmatic dependent of the kernel before it.  The weights
-  // are static: the first chunks of this warp's first row are loaded into
-  // registers before waiting for that kernel (which writes x / the residual)
-  // and while x is staged.
+  const int64_t ksteps = K / 16;
   // (with the all-reduce, later kernels are not placed early: they could take
   // the space of CTAs that other ranks' CTAs are waiting for)
   if (!AR) asm volatile("griddepcontrol.launch_dependents;");
-  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kGemvWarps + warp;
-  uint4 wv[kGemvUnroll], wv2[kGemvUnroll];  // weight chunks in flight
+
+  // ---- work: a CTA iteration covers (kGemvWarps / ksplit) row blocks of 16
+  //      rows; a block's K is split over ksplit warps ----
+  const int ksplit = a.ksplit;
+  const int rpi = (kGemvWarps / ksplit) * 16;
+  const int wrow = warp / ksplit, ws = warp - (warp / ksplit) * ksplit;
+  const int64_t kss = (ksteps + ksplit - 1) / ksplit;
+  const int64_t ks_begin = ws * kss, ks_end = min(ksteps, ks_begin + kss);
+  const int nj = static_cast<int>((kss + kU - 1) / kU);  // items per row block
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * rpi;
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * rpi;
+  const int n_groups = first < a.n ? static_cast<int>((a.n - first + gstride - 1) / gstride) : 0;
+  const int total = n_groups * nj;
+
+  auto slot_addr = [&](int r, int stream, int u) -> uint32_t {
+    return ring + static_cast<uint32_t>((((r * kStreams + stream) * kU + u) * kGemvThreads +
+                                         threadIdx.x) * 16);
+  };
+  int issued = 0, ig = 0, jg = 0, ir = 0;
+  auto issue_next = [&]() {
+    if (issued < total) {
+      const int64_t rowc = first + ig * gstride + wrow * 16 + (lane & 15);
 #pragma unroll
-  for (int u = 0; u < kGemvUnroll; ++u) {
-    const int64_t c = lane + u * 32;
-    if (row0 < a.n && c < chunks) {
-      wv[u] = ld_stream_v4(W + row0 * K + c * 8);
-      if (glu) wv2[u] = ld_stream_v4(W2 + row0 * K + c * 8);
+      for (int u = 0; u < kU; ++u) {
+        const int64_t kst = ks_begin + jg * kU + u;
+        const bool ok = rowc < a.n && kst < ks_end;
+        const int64_t off = ok ? rowc * K + kst * 16 + (lane >> 4) * 8 : 0;
+        cp_async_16(slot_addr(ir, 0, u), W + off, ok ? 16u : 0u);
+        if (GLU) cp_async_16(slot_addr(ir, 1, u), W2 + off, ok ? 16u : 0u);
+      }
+      ++issued;
+      if (++jg == nj) {
+        jg = 0;
+        ++ig;
+      }
+      if (++ir == kDepth) ir = 0;
     }
-  }
+    cp_async_commit();  // one group per item (empty past the end): uniform wait counts
+  };
+  // the weights are static: fill the ring before waiting for the kernel before
+  // this one (which writes x / the residual) and while x is staged
+#pragma unroll 1
+  for (int i = 0; i < kDepth - 1; ++i) issue_next();
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // all-reduce: this CTA's epoch (one counter per CTA index, same rows on
   // every rank), advanced at the end of the call
@@ -204,12 +267,12 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, AR ? 1 : GemvShape<NB
   // ---- stage x (rows >= batch are zero), RMSNorm'd when norm_w is given ----
   for (int b = 0; b < NB; ++b) {
     if (b >= a.batch) {
-      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * K + i] = from_float<T>(0.f);
+      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = from_float<T>(0.f);
       continue;
     }
     const T* xb = x + b * a.x_stride;
     if (nw == nullptr) {
-      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * K + i] = xb[i];
+      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = xb[i];
       continue;
     }
     float ss = 0.f;
@@ -230,113 +293,398 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, AR ? 1 : GemvShape<NB
     const float sc = s_scale;
     for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
       const float xn = round_to<T>(to_float<T>(xb[i]) * sc);        // x.to(dtype)
-      xs[b * K + i] = from_float<T>(to_float<T>(nw[i]) * xn);      // weight * x
+      xs[b * XS + i] = from_float<T>(to_float<T>(nw[i]) * xn);     // weight * x
     }
     __syncthreads();
   }
   __syncthreads();
 
-  // ---- one output row per warp at a time ----
-  bool preloaded = true;
-  for (int64_t row = row0; row < a.n; row += static_cast<int64_t>(gridDim.x) * kGemvWarps) {
-    float acc[NB], acc2[NB];
+  float acc[NT][4], acc2[NT][4];
 #pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
-    const T* wr = W + row * K;
-    const T* wr2 = glu ? W2 + row * K : nullptr;
-    for (int64_t c0 = lane; c0 < chunks; c0 += 32 * kGemvUnroll) {
-      if (preloaded) {  // the first chunk group of the first row is in flight already
-        preloaded = false;
-      } else {
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-          const int64_t c = c0 + u * 32;
-          if (c < chunks) {
-            wv[u] = ld_stream_v4(wr + c * 8);
-            if (glu) wv2[u] = ld_stream_v4(wr2 + c * 8);
+    for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[nt][e] = 0.f;
+  int g = 0, j = 0, cr = 0;  // consume pointer: row group, item in the block, ring slot
+#pragma unroll 1
+  for (int i = 0; i < total; ++i) {
+    issue_next();
+    cp_async_wait<kDepth - 1>();  // this lane's copies of item i have landed
+    __syncwarp();                 // ... and every lane's, before ldmatrix reads them
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t kst = ks_begin + j * kU + u;
+      if (kst < ks_end) {  // uniform over the warp
+        uint32_t af[4];
+        ldsm_x4(slot_addr(cr, 0, u), af[0], af[1], af[2], af[3]);
+        uint32_t af2[4];
+        if (GLU) ldsm_x4(slot_addr(cr, 1, u), af2[0], af2[1], af2[2], af2[3]);
+        const int64_t kk = kst * 16 + 2 * tq;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int col = nt * 8 + gq;
+          uint32_t b0 = 0u, b1 = 0u;
+          if (col < NB) {
+            b0 = *reinterpret_cast<const uint32_t*>(xs + col * XS + kk);
+            b1 = *reinterpret_cast<const uint32_t*>(xs + col * XS + kk + 8);
+          }
+          MmaOp<T>::run(acc[nt], af, b0, b1);
+          if (GLU) MmaOp<T>::run(acc2[nt], af2, b0, b1);
+        }
+      }
+    }
+    __syncwarp();  // all lanes have read item i's slots before they are refilled
+    if (++cr == kDepth) cr = 0;
+    const bool block_done = ++j == nj;
+    if (block_done) {
+      j = 0;
+      ++g;
+    }
+    if (!block_done) continue;
+    // ---- end of row group: combine the K slices, epilogue ----
+    // thread (gq, tq) holds rows gq / gq + 8, columns nt*8 + 2tq (+1)
+    const int64_t rb = first + (g - 1) * gstride + wrow * 16;
+    if (ksplit > 1) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = gq + (e >> 1) * 8, c = nt * 8 + 2 * tq + (e & 1);
+          if (c < NB) {
+            s_part[warp][r][c][0] = acc[nt][e];
+            if (GLU) s_part[warp][r][c][kStreams - 1] = acc2[nt][e];
           }
         }
-      }
+      __syncthreads();
+      if (ws == 0) {
 #pragma unroll
-      for (int u = 0; u < kGemvUnroll; ++u) {
-        const int64_t c = c0 + u * 32;
-        if (c < chunks) {
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xs + b * K + c * 8);
-            acc[b] += dot8<T>(wv[u], xv);
-            if (glu) acc2[b] += dot8<T>(wv2[u], xv);
+          for (int e = 0; e < 4; ++e) {
+            const int r = gq + (e >> 1) * 8, c = nt * 8 + 2 * tq + (e & 1);
+            if (c < NB) {
+              float t = 0.f, t2 = 0.f;
+              for (int q = 0; q < ksplit; ++q) {
+                t += s_part[warp + q][r][c][0];
+                if (GLU) t2 += s_part[warp + q][r][c][kStreams - 1];
+              }
+              acc[nt][e] = t;
+              acc2[nt][e] = t2;
+            }
           }
+      }
+      __syncthreads();
+    }
+    if (ws == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t row = rb + gq + (e >> 1) * 8;
+          const int b = nt * 8 + 2 * tq + (e & 1);
+          if (b >= a.batch || row >= a.n) continue;
+          float dot = acc[nt][e];
+          if (AR) {  // sum the ranks' partial dot products before rounding
+            float sum = 0.f;
+            if (!allreduce_value(a, s_epoch, row, b, dot, sum)) {
+              atomicExch(&s_ar_ok, 0);
+              continue;
+            }
+            dot = sum;
+          }
+          float v = round_to<T>(dot);  // projection output in the model dtype
+          if (GLU) {
+            const float up = round_to<T>(acc2[nt][e]);
+            const float sg = round_to<T>(v / (1.f + expf(-v)));  // act_fn(gate)
+            v = round_to<T>(sg * up);
+          }
+          if (a.residual != nullptr)
+            v = round_to<T>(to_float<T>(static_cast<const T*>(a.residual)[b * a.res_stride + row]) + v);
+          if (a.y_fp32)
+            static_cast<float*>(a.y)[b * a.y_stride + row] = v;
+          else
+            static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
         }
-      }
     }
 #pragma unroll
-    for (int b = 0; b < NB; ++b) {
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
-        if (glu) acc2[b] += __shfl_xor_sync(0xffffffffu, acc2[b], o);
-      }
-    }
-    // lane b writes batch row b
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-      if (lane != b || b >= a.batch) continue;
-      if (AR) {  // sum the ranks' partial dot products before rounding
-        float sum = 0.f;
-        if (!allreduce_value(a, s_epoch, row, b, acc[b], sum)) {
-          atomicExch(&s_ar_ok, 0);
-          continue;
-        }
-        acc[b] = sum;
-      }
-      float v = round_to<T>(acc[b]);  // projection output in the model dtype
-      if (glu) {
-        const float u = round_to<T>(acc2[b]);
-        const float s = round_to<T>(v / (1.f + expf(-v)));  // act_fn(gate)
-        v = round_to<T>(s * u);
-      }
-      if (a.residual != nullptr)
-        v = round_to<T>(to_float<T>(static_cast<const T*>(a.residual)[b * a.res_stride + row]) + v);
-      if (a.y_fp32)
-        static_cast<float*>(a.y)[b * a.y_stride + row] = v;
-      else
-        static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
-    }
+      for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[nt][e] = 0.f;
   }
+  cp_async_wait<0>();
   if (AR) {
     __syncthreads();
     if (threadIdx.x == 0 && s_ar_ok) reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] = s_epoch;
   }
 }
 
-template <typename T, int NB, bool AR>
+// Narrow batches (1-2 rows): one weight row per warp (split along K over
+// ksplit warps for long rows), CUDA-core FMAs on 16-byte chunks; the same
+// cp.async ring, each lane reading back only the chunks it copied.  Finer
+// work units than the 16-row blocks of the tensor-core form, which matters
+// when one row of x leaves the tensor cores idle anyway.
+template <typename T, int NB, bool AR, bool GLU>
+__global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_kernel(const GemvArgs a) {
+  constexpr int kGemvThreads = GemvShape<NB>::kThreads;
+  constexpr int kGemvWarps = GemvShape<NB>::kWarps;
+  constexpr int kStreams = GLU ? 2 : 1;
+  constexpr int kU = GLU ? 2 : 4;  // 16-byte chunks per lane (and stream) per ring item
+  constexpr int kDepth = GemvShape<NB>::kRingPerLane / (16 * kU * kStreams);
+  static_assert(kDepth >= 2, "ring needs two items");
+  extern __shared__ __align__(128) uint8_t gemv_smem[];
+  const int64_t K = a.k;
+  const int64_t XS = gemv_x_stride<NB>(K);
+  T* xs = reinterpret_cast<T*>(gemv_smem);  // [NB][XS]
+  const uint32_t ring = smem_addr(gemv_smem) +
+                        static_cast<uint32_t>((NB * XS * sizeof(T) + 127) / 128 * 128);
+  __shared__ float s_red[kGemvWarps];
+  __shared__ float s_scale;
+  __shared__ float s_part[kGemvWarps][NB][2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* x = static_cast<const T*>(a.x);
+  const T* nw = static_cast<const T*>(a.norm_w);
+  const T* W = static_cast<const T*>(a.w);
+  const T* W2 = static_cast<const T*>(a.w2);
+  const int64_t chunks = K / 8;  // 16-byte chunks per row
+  if (!AR) asm volatile("griddepcontrol.launch_dependents;");
+  const int ksplit = a.ksplit;              // warps per row (divides kGemvWarps)
+  const int rpi = kGemvWarps / ksplit;      // rows per CTA iteration
+  const int wrow = warp / ksplit, ws = warp - (warp / ksplit) * ksplit;
+  const int64_t cs = (chunks + ksplit - 1) / ksplit;
+  const int64_t c_begin = ws * cs, c_end = min(chunks, c_begin + cs);
+  const int nj = static_cast<int>((cs + 32 * kU - 1) / (32 * kU));  // items per row
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * rpi;
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * rpi;
+  const int n_groups = first < a.n ? static_cast<int>((a.n - first + gstride - 1) / gstride) : 0;
+  const int total = n_groups * nj;
+  auto slot_addr = [&](int r, int stream, int u) -> uint32_t {
+    return ring + static_cast<uint32_t>((((r * kStreams + stream) * kU + u) * kGemvThreads +
+                                         threadIdx.x) * 16);
+  };
+  int issued = 0, ig = 0, jg = 0, ir = 0;
+  auto issue_next = [&]() {
+    if (issued < total) {
+      const int64_t row = first + ig * gstride + wrow;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t c = c_begin + lane + 32 * (jg * kU + u);
+        const bool ok = row < a.n && c < c_end;
+        const int64_t off = ok ? row * K + c * 8 : 0;
+        cp_async_16(slot_addr(ir, 0, u), W + off, ok ? 16u : 0u);
+        if (GLU) cp_async_16(slot_addr(ir, 1, u), W2 + off, ok ? 16u : 0u);
+      }
+      ++issued;
+      if (++jg == nj) {
+        jg = 0;
+        ++ig;
+      }
+      if (++ir == kDepth) ir = 0;
+    }
+    cp_async_commit();
+  };
+#pragma unroll 1
+  for (int i = 0; i < kDepth - 1; ++i) issue_next();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_ar_ok;
+  if (AR && threadIdx.x == 0) {
+    s_epoch = reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] + 1u;
+    s_ar_ok = 1;
+  }
+  for (int b = 0; b < NB; ++b) {
+    if (b >= a.batch) {
+      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = from_float<T>(0.f);
+      continue;
+    }
+    const T* xb = x + b * a.x_stride;
+    if (nw == nullptr) {
+      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = xb[i];
+      continue;
+    }
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
+      const float v = to_float<T>(xb[i]);
+      ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.f;
+      for (int w = 0; w < kGemvWarps; ++w) t += s_red[w];
+      s_scale = rsqrtf(t / static_cast<float>(K) + a.eps);
+    }
+    __syncthreads();
+    const float sc = s_scale;
+    for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
+      const float xn = round_to<T>(to_float<T>(xb[i]) * sc);
+      xs[b * XS + i] = from_float<T>(to_float<T>(nw[i]) * xn);
+    }
+    __syncthreads();
+  }
+  __syncthreads();
+  float acc[NB], acc2[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
+  int g = 0, j = 0, cr = 0;
+#pragma unroll 1
+  for (int i = 0; i < total; ++i) {
+    issue_next();
+    cp_async_wait<kDepth - 1>();
+    const int64_t row = first + g * gstride + wrow;
+    if (row < a.n) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t c = c_begin + lane + 32 * (j * kU + u);
+        if (c < c_end) {
+          uint4 wv, wv2;
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(wv.x), "=r"(wv.y), "=r"(wv.z), "=r"(wv.w)
+                       : "r"(slot_addr(cr, 0, u)));
+          if (GLU)
+            asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(wv2.x), "=r"(wv2.y), "=r"(wv2.z), "=r"(wv2.w)
+                         : "r"(slot_addr(cr, 1, u)));
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xs + b * XS + c * 8);
+            acc[b] += dot8<T>(wv, xv);
+            if (GLU) acc2[b] += dot8<T>(wv2, xv);
+          }
+        }
+      }
+    }
+    if (++cr == kDepth) cr = 0;
+    const bool row_done = ++j == nj;
+    if (row_done) {
+      j = 0;
+      ++g;
+    }
+    if (!row_done) continue;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        acc[b] += __shfl_xor_sync(0xffffffffu, acc[b], o);
+        if (GLU) acc2[b] += __shfl_xor_sync(0xffffffffu, acc2[b], o);
+      }
+    }
+    if (ksplit > 1) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        if (lane == b) {
+          s_part[warp][b][0] = acc[b];
+          s_part[warp][b][1] = acc2[b];
+        }
+      __syncthreads();
+      if (ws == 0) {
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          if (lane == b) {
+            float t = 0.f, t2 = 0.f;
+            for (int q = 0; q < ksplit; ++q) {
+              t += s_part[warp + q][b][0];
+              t2 += s_part[warp + q][b][1];
+            }
+            acc[b] = t;
+            acc2[b] = t2;
+          }
+      }
+      __syncthreads();
+    }
+    if (ws == 0 && row < a.n) {
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (lane != b || b >= a.batch) continue;
+        float dot = acc[b];
+        if (AR) {
+          float sum = 0.f;
+          if (!allreduce_value(a, s_epoch, row, b, dot, sum)) {
+            atomicExch(&s_ar_ok, 0);
+            continue;
+          }
+          dot = sum;
+        }
+        float v = round_to<T>(dot);
+        if (GLU) {
+          const float up = round_to<T>(acc2[b]);
+          const float sg = round_to<T>(v / (1.f + expf(-v)));
+          v = round_to<T>(sg * up);
+        }
+        if (a.residual != nullptr)
+          v = round_to<T>(to_float<T>(static_cast<const T*>(a.residual)[b * a.res_stride + row]) + v);
+        if (a.y_fp32)
+          static_cast<float*>(a.y)[b * a.y_stride + row] = v;
+        else
+          static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
+  }
+  cp_async_wait<0>();
+  if (AR) {
+    __syncthreads();
+    if (threadIdx.x == 0 && s_ar_ok) reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] = s_epoch;
+  }
+}
+
+template <typename T, int NB, bool AR, bool GLU>
 int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
-  static unsigned long long configured = 0;
+  // narrow batches: CUDA-core form with one row per warp; wider: tensor cores
+  constexpr bool kMma = NB >= 4;
+  auto kernel = kMma ? decode_gemv_kernel<T, NB, AR, GLU> : decode_gemv_cc_kernel<T, NB, AR, GLU>;
+  static size_t configured[64] = {0};  // dynamic smem allowed so far, per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return HELM_ERR_CUDA;
-  const size_t smem = static_cast<size_t>(NB) * a.k * sizeof(T);
-  if (smem > 200 * 1024) return HELM_ERR_UNSUPPORTED;
-  if (!(configured & (1ull << dev))) {
-    if (cudaFuncSetAttribute(decode_gemv_kernel<T, NB, AR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             200 * 1024) != cudaSuccess)
+  const size_t smem = gemv_smem_bytes<T, NB>(a.k);
+  // dynamic + static (the K-slice partials) shared memory of one CTA
+  if (smem + sizeof(float) * GemvShape<NB>::kWarps * 16 * NB * 2 + 1024 > kGemvMaxSmem)
+    return HELM_ERR_UNSUPPORTED;
+  if (smem > configured[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
       return HELM_ERR_CUDA;
-    configured |= 1ull << dev;
+    configured[dev] = smem;
   }
-  int per_sm = smem <= 48 * 1024 ? 4 : (smem <= 100 * 1024 ? 2 : 1);
-  if (AR) {
-    // every CTA must be resident at once: CTA c waits for CTA c of the other
-    // ranks, whose own CTAs may wait for ours
-    int fit = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, decode_gemv_kernel<T, NB, AR>,
-                                                      GemvShape<NB>::kThreads, smem) != cudaSuccess ||
-        fit <= 0)
-      return HELM_ERR_CUDA;
-    per_sm = std::min(per_sm, fit);
-  }
+  // one wave of resident CTAs looping over row groups (with the all-reduce,
+  // every CTA must be resident at once: CTA c waits for CTA c of the other
+  // ranks, whose own CTAs may wait for ours)
+  int fit = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, kernel, GemvShape<NB>::kThreads, smem) !=
+          cudaSuccess ||
+      fit <= 0)
+    return HELM_ERR_CUDA;
   constexpr int kWarps = GemvShape<NB>::kWarps;
-  const int64_t want = (a.n + kWarps - 1) / kWarps;
-  const int grid = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms_current_device()) * per_sm));
+  GemvArgs args = a;
+  // K split over ksplit warps of a CTA, chosen to minimise the busiest warp's
+  // ring items: ceil(row groups / CTAs) x ceil(K slice / item width), where an
+  // item is 32 lanes x kU chunks (CUDA-core form) or kU k-steps of a 16-row
+  // block (tensor cores); each extra split adds a barrier per row group
+  const int grid_max = num_sms_current_device() * fit;
+  const int unit = kMma ? 16 : 1;  // rows of one warp task
+  const int64_t k_units = kMma ? a.k / 16 : a.k / 8;
+  const int64_t item_units = kMma ? (GLU ? 2 : 4) : 32 * (GLU ? 2 : 4);
+  int ks = 1;
+  double best = 1e30;
+  for (int c = 1; c <= kWarps; c *= 2) {
+    const int64_t slice = (k_units + c - 1) / c;
+    if (c > 1 && slice < item_units) break;
+    const int64_t rows_per_group = static_cast<int64_t>(kWarps / c) * unit;
+    const int64_t groups = (a.n + rows_per_group - 1) / rows_per_group;
+    const int64_t iters = (groups + grid_max - 1) / grid_max;
+    const double cost = static_cast<double>(iters) *
+                        (static_cast<double>((slice + item_units - 1) / item_units) +
+                         (c > 1 ? 0.5 : 0.0));
+    if (cost < best) {
+      best = cost;
+      ks = c;
+    }
+  }
+  args.ksplit = ks;
+  const int rpi = (kWarps / ks) * unit;
+  const int64_t want = (a.n + rpi - 1) / rpi;
+  const int grid = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms_current_device()) * fit));
   if (AR && grid * 4 > kArHeaderBytes) return HELM_ERR_UNSUPPORTED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -348,17 +696,23 @@ int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_gemv_kernel<T, NB, AR>, a) == cudaSuccess ? HELM_OK
-                                                                                : HELM_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, kernel, args) == cudaSuccess
+             ? HELM_OK
+             : HELM_ERR_CUDA;
+}
+
+template <typename T, int NB, bool AR>
+int launch_gemv_glu(const GemvArgs& a, cudaStream_t s) {
+  return a.w2 != nullptr ? launch_gemv<T, NB, AR, true>(a, s) : launch_gemv<T, NB, AR, false>(a, s);
 }
 
 template <typename T, bool AR>
 int dispatch_gemv(const GemvArgs& a, cudaStream_t s) {
-  if (a.batch <= 1) return launch_gemv<T, 1, AR>(a, s);
-  if (a.batch <= 2) return launch_gemv<T, 2, AR>(a, s);
-  if (a.batch <= 4) return launch_gemv<T, 4, AR>(a, s);
-  if (a.batch <= 8) return launch_gemv<T, 8, AR>(a, s);
-  return launch_gemv<T, 16, AR>(a, s);
+  if (a.batch <= 1) return launch_gemv_glu<T, 1, AR>(a, s);
+  if (a.batch <= 2) return launch_gemv_glu<T, 2, AR>(a, s);
+  if (a.batch <= 4) return launch_gemv_glu<T, 4, AR>(a, s);
+  if (a.batch <= 8) return launch_gemv_glu<T, 8, AR>(a, s);
+  return launch_gemv_glu<T, 16, AR>(a, s);
 }
 
 
@@ -416,7 +770,7 @@ int gemv_entry(const void* x, int64_t x_stride, const void* norm_w, float eps, c
   if (batch <= 0 || n <= 0 || k <= 0) return HELM_ERR_INVALID_ARGUMENT;
   if (batch > 16) return HELM_ERR_UNSUPPORTED;
   if (dtype != HELM_DTYPE_BF16 && dtype != HELM_DTYPE_FP16) return HELM_ERR_UNSUPPORTED;
-  if (k % 8 != 0) return HELM_ERR_UNSUPPORTED;
+  if (k % 16 != 0) return HELM_ERR_UNSUPPORTED;
   if ((reinterpret_cast<uintptr_t>(w) & 15) || (w2 != nullptr && (reinterpret_cast<uintptr_t>(w2) & 15)))
     return HELM_ERR_ALIGNMENT;
   GemvArgs a;

@@ -97,6 +97,16 @@ class FusedDecodeStage:
         self.qkv = torch.empty(B, n_qkv, dtype=self.dtype, device=self.dev)
         self.act = torch.empty(B, inter, dtype=self.dtype, device=self.dev)
 
+    @staticmethod
+    def _gemv(x, w, out, **kw):
+        """helm_decode_gemv over batch slices whose inputs fit its staging."""
+        n = _capi.gemv_max_batch(x.shape[1], x.element_size())
+        res = kw.pop("residual", None)
+        for b0 in range(0, x.shape[0], n):
+            b1 = min(x.shape[0], b0 + n)
+            _capi.decode_gemv(x[b0:b1], w, out=out[b0:b1],
+                              residual=None if res is None else res[b0:b1], **kw)
+
     @torch.no_grad()
     def step(self, ids: torch.Tensor, pos: torch.Tensor, logits: torch.Tensor, ctx) -> None:
         """ids, pos [B, 1] (device); writes logits [B, vocab].  ctx: the
@@ -108,7 +118,7 @@ class FusedDecodeStage:
         cos, sin = cos.reshape(B, D), sin.reshape(B, D)
         pool = ctx.pool.storage
         for l, w in enumerate(self.layers):
-            _capi.decode_gemv(h, w.wqkv, out=qkv, norm_w=w.ln1, eps=w.eps1)
+            self._gemv(h, w.wqkv, qkv, norm_w=w.ln1, eps=w.eps1)
             q = qkv[:, :w.nq].view(B, Hq, D)
             k = qkv[:, w.nq:w.nq + w.nk].view(B, -1, D)
             v = qkv[:, w.nq + w.nk:].view(B, -1, D)
@@ -121,7 +131,7 @@ class FusedDecodeStage:
                                          scale=D ** -0.5, out=ctx.attn_out[l],
                                          max_kv_len_hint=ctx.max_len)
             ctx.after_attention(l)
-            _capi.decode_gemv(ctx.attn_out[l].view(B, Hq * D), w.wo, out=h, residual=h)
-            _capi.decode_gemv(h, w.wg, w2=w.wu, out=act, norm_w=w.ln2, eps=w.eps2)
-            _capi.decode_gemv(act, w.wd, out=h, residual=h)
-        _capi.decode_gemv(h, self.lm_head, out=logits, norm_w=self.final_norm, eps=self.final_eps)
+            self._gemv(ctx.attn_out[l].view(B, Hq * D), w.wo, h, residual=h)
+            self._gemv(h, w.wg, act, w2=w.wu, norm_w=w.ln2, eps=w.eps2)
+            self._gemv(act, w.wd, h, residual=h)
+        self._gemv(h, self.lm_head, logits, norm_w=self.final_norm, eps=self.final_eps)

@@ -185,6 +185,7 @@ class TPDecodeModel:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.dev = w.embed.device
         self.dtype = w.embed.dtype
+        self.embed_elem = w.embed.element_size()
         self.B, self.P, self.D = batch, page_size, w.head_dim
         self.L = len(w.layers)
         self.H = w.embed.shape[1]
@@ -231,12 +232,23 @@ class TPDecodeModel:
             self.peers = None
 
     # ------------------------------------------------------------------- step --
+    def _slices(self, k: int):
+        """Batch slices whose inputs helm_decode_gemv can stage (batch x k)."""
+        n = _capi.gemv_max_batch(k, self.embed_elem)
+        return [(b, min(self.B, b + n)) for b in range(0, self.B, n)]
+
+    def _gemv(self, x, w, out, norm_w=None, eps=1e-6, w2=None):
+        for b0, b1 in self._slices(x.shape[1]):
+            _capi.decode_gemv(x[b0:b1], w, out=out[b0:b1], norm_w=norm_w, eps=eps, w2=w2)
+
     def _row_proj(self, x, w, out):
         """out = out + (row-parallel) W x, all-reduced over the ranks."""
-        if self.peers is None:
-            _capi.decode_gemv(x, w, out=out, residual=out)
-        else:
-            _capi.decode_gemv_allreduce(self.peers.ptrs, self.rank, x, w, out=out, residual=out)
+        for b0, b1 in self._slices(x.shape[1]):
+            if self.peers is None:
+                _capi.decode_gemv(x[b0:b1], w, out=out[b0:b1], residual=out[b0:b1])
+            else:
+                _capi.decode_gemv_allreduce(self.peers.ptrs, self.rank, x[b0:b1], w,
+                                            out=out[b0:b1], residual=out[b0:b1])
 
     @torch.no_grad()
     def step(self, forced: Optional[torch.Tensor] = None) -> None:
@@ -257,7 +269,7 @@ class TPDecodeModel:
         lens1 = self.lens + 1
         scale = D ** -0.5
         for l, lw in enumerate(w.layers):
-            _capi.decode_gemv(h, lw.wqkv, out=self.qkv, norm_w=lw.ln1, eps=lw.eps1)
+            self._gemv(h, lw.wqkv, self.qkv, norm_w=lw.ln1, eps=lw.eps1)
             nq, nk = w.hq * D, w.hkv * D
             q = self.qkv[:, :nq].view(B, w.hq, D)
             k = self.qkv[:, nq:nq + nk].view(B, w.hkv, D)
@@ -269,9 +281,9 @@ class TPDecodeModel:
                                          num_kv_heads=w.hkv, page_size=P, scale=scale,
                                          out=self.attn, max_kv_len_hint=self.max_len)
             self._row_proj(self.attn.view(B, w.hq * D), lw.wo, h)
-            _capi.decode_gemv(h, lw.wg, w2=lw.wu, out=self.act, norm_w=lw.ln2, eps=lw.eps2)
+            self._gemv(h, lw.wg, self.act, norm_w=lw.ln2, eps=lw.eps2, w2=lw.wu)
             self._row_proj(self.act, lw.wd, h)
-        _capi.decode_gemv(h, w.lm_head, out=self.logits, norm_w=w.final_norm, eps=w.final_eps)
+        self._gemv(h, w.lm_head, self.logits, norm_w=w.final_norm, eps=w.final_eps)
         # greedy pick over the vocab shards: (max value, global index) per rank
         val, idx = self.logits.float().max(dim=-1)
         local = torch.stack([val, (idx + self.rank * w.lm_head.shape[0]).float()], dim=-1)

@@ -283,8 +283,9 @@ int helm_seq_exchange_merge(void* const* bufs, int rank, int world, const float*
  *   y[b] = residual[b] + W x[b]     when residual != NULL
  * (norm and SwiGLU/residual may be combined), rounding to `dtype` where HF's
  * eager modules do.  x [batch, k] (row stride x_stride elements), W / W2
- * [n, k] row-major 16-byte aligned, k % 8 == 0, batch <= 16, batch * k * 2
- * bytes <= 200 KiB; y [batch, n] (row stride y_stride) in dtype, or fp32 when
+ * [n, k] row-major 16-byte aligned, k % 16 == 0, batch <= 16, x of all batch
+ * rows fits the CTA's shared memory (about batch * k * 2 bytes <= 190 KiB, less
+ * for 8+ rows); y [batch, n] (row stride y_stride) in dtype, or fp32 when
  * y_fp32.  y may alias residual.  dtype: HELM_DTYPE_BF16 or HELM_DTYPE_FP16.
  */
 int helm_decode_gemv(const void* x, int64_t x_stride, const void* norm_w, float eps,

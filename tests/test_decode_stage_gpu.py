@@ -31,7 +31,8 @@ def dev():
 
 
 @pytest.mark.parametrize("B,N,K", [(1, 1000, 512), (3, 777, 1024), (8, 256, 2048),
-                                   (16, 130, 640)])
+                                   (16, 130, 640), (2, 300, 9008), (1, 513, 17408),
+                                   (4, 100, 5120)])
 def test_gemv_variants_vs_fp32(dev, B, N, K):
     g = torch.Generator(device=dev).manual_seed(B * 7 + N)
     x = torch.randn(B, K, device=dev, generator=g).to(torch.bfloat16)
