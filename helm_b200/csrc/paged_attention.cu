@@ -699,19 +699,23 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
 }
 
 // Merges the pairs whose tiles were split across CTAs (second kernel of a
-// call).  CTA (pair p, chunk) owns up to kMergeThreads float4 elements of p's
-// G x D output block.  Its sources are the CTA partials of CTAs
+// call).  CTA (pair p, chunk) owns 32 float4 elements of p's G x D output
+// block, one per lane.  Its sources are the CTA partials of CTAs
 // vf/NCW .. vl_end/NCW (slots c + p) and, when the pair's last worker
-// continues into the next pair, that worker's partial (slot vl + p).  Each
-// thread loads (m, l) and O of up to kMergeBatch sources at once, rescaling
-// its running state between batches, so a pair costs one dependent L2 round
-// trip per kMergeBatch sources.
-constexpr int kMergeThreads = 128;
-constexpr int kMergeBatch = 16;
+// continues into the next pair, that worker's partial (slot vl + p).  The
+// kMergeWarps warps take disjoint subsets of the sources (loads of up to
+// kMergeBatch sources in flight per lane, a running rescaled state between
+// batches); their states meet in shared memory.  With few long sequences a
+// pair has dozens of sources, so spreading them over warps keeps the merge at
+// one or two L2 round trips.
+constexpr int kMergeWarps = 8;
+constexpr int kMergeThreads = kMergeWarps * 32;
+constexpr int kMergeBatch = 8;
 
 template <typename T, int D, int NCW>
-__global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kMergeThreads, 4) merge_split_pairs_kernel(const DecodeArgs a) {
   extern __shared__ int s_cum_m[];
+  __shared__ float s_st[kMergeWarps][6][32];  // per warp: M, L, acc.xyzw per lane
   asm volatile("griddepcontrol.launch_dependents;");
   const int p = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -730,17 +734,18 @@ __global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const 
   const int K = n_cta + (ps.last_continues ? 1 : 0);
   const int G = a.group;
   constexpr int D4 = D / 4;
-  const int e = blockIdx.y * kMergeThreads + threadIdx.x;
-  if (e >= G * D4) return;
-  const int hg = e / D4, d4 = e - (e / D4) * D4;
+  const int e = blockIdx.y * 32 + lane;
+  const bool active = e < G * D4;
+  const int hg = active ? e / D4 : 0, d4 = active ? e - (e / D4) * D4 : 0;
   float M = -INFINITY, Lsum = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int k0 = 0; k0 < K; k0 += kMergeBatch) {
+  // warp w: sources w, w + kMergeWarps, ...
+  for (int k0 = warp; active && k0 < K; k0 += kMergeWarps * kMergeBatch) {
     float2 ml[kMergeBatch];
     float4 o[kMergeBatch];
 #pragma unroll
     for (int i = 0; i < kMergeBatch; ++i) {  // issue the whole batch first
-      const int k = k0 + i;
+      const int k = k0 + i * kMergeWarps;
       ml[i] = make_float2(-INFINITY, 0.f);
       o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k < K) {
@@ -774,15 +779,37 @@ __global__ void __launch_bounds__(kMergeThreads) merge_split_pairs_kernel(const 
     }
     M = Mb;
   }
+  s_st[warp][0][lane] = M;
+  s_st[warp][1][lane] = Lsum;
+  s_st[warp][2][lane] = acc.x;
+  s_st[warp][3][lane] = acc.y;
+  s_st[warp][4][lane] = acc.z;
+  s_st[warp][5][lane] = acc.w;
+  __syncthreads();
+  if (warp != 0 || !active) return;
+  float Mt = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, s_st[w][0][lane]);
+  const float m_use = Mt == -INFINITY ? 0.f : Mt;
+  float L = 0.f, ox = 0.f, oy = 0.f, oz = 0.f, ow = 0.f;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) {
+    const float f = exp2f(s_st[w][0][lane] - m_use);  // 0 for warps without sources
+    L += s_st[w][1][lane] * f;
+    ox += s_st[w][2][lane] * f;
+    oy += s_st[w][3][lane] * f;
+    oz += s_st[w][4][lane] * f;
+    ow += s_st[w][5][lane] * f;
+  }
   const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
-  const float inv = 1.f / fmaxf(Lsum, 1e-12f);
-  store_out<T>(a, b, h * G + hg, d4 * 4 + 0, acc.x * inv);
-  store_out<T>(a, b, h * G + hg, d4 * 4 + 1, acc.y * inv);
-  store_out<T>(a, b, h * G + hg, d4 * 4 + 2, acc.z * inv);
-  store_out<T>(a, b, h * G + hg, d4 * 4 + 3, acc.w * inv);
+  const float inv = 1.f / fmaxf(L, 1e-12f);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 0, ox * inv);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 1, oy * inv);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 2, oz * inv);
+  store_out<T>(a, b, h * G + hg, d4 * 4 + 3, ow * inv);
   if (d4 == 0 && a.lse != nullptr)
     a.lse[static_cast<int64_t>(b) * a.hq + h * G + hg] =
-        (M == -INFINITY || Lsum <= 0.f) ? -INFINITY : M * kLn2 + logf(Lsum);
+        (Mt == -INFINITY || L <= 0.f) ? -INFINITY : Mt * kLn2 + logf(L);
 }
 
 // ----------------------------------------------------------------- host side --
@@ -854,7 +881,7 @@ int launch(const DecodeArgs& a, const void* pool, int64_t pool_rows, int grid,
   // merge of split pairs: a programmatic dependent of the decode kernel
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.hkv),
-                     static_cast<unsigned>((a.group * (D / 4) + kMergeThreads - 1) / kMergeThreads));
+                     static_cast<unsigned>((a.group * (D / 4) + 31) / 32));
   cfg.blockDim = dim3(kMergeThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(a.batch + 1) * sizeof(int);
   cfg.stream = stream;
