@@ -126,12 +126,14 @@ __device__ __forceinline__ uint64_t gemv_timer_ns() {
 
 // All-reduce of one output value over the ranks (tensor-parallel row-parallel
 // projection).  Words {fp32 value, epoch} [2 parities][world][n][batch] in
-// every rank's buffer; this lane stores its partial for (row, b) into slot
-// `rank` of every buffer, then polls its own buffer for all ranks' partials of
-// (row, b) and returns their sum in rank order (the same on every rank).
-// Returns false when the poll ran out of time (status word set).
-__device__ __forceinline__ bool allreduce_value(const GemvArgs& a, uint32_t e, int64_t row, int b,
-                                                float part, float& sum) {
+// every rank's buffer.  ar_push stores this rank's partial for (row, b) into
+// slot `rank` of every buffer (NVLink stores, no wait); ar_poll later reads
+// all ranks' partials of (row, b) from this rank's buffer and returns their
+// sum in rank order (the same on every rank), or false when the poll ran out
+// of time (status word set).  Pushing every row first and polling afterwards
+// costs one NVLink round trip per call instead of one per row group.
+__device__ __forceinline__ void ar_push(const GemvArgs& a, uint32_t e, int64_t row, int b,
+                                        float part) {
   const int par = static_cast<int>(e & 1u);
   const int64_t slot_words = a.n * a.batch;
   const int64_t off = row * a.batch + b;
@@ -140,10 +142,16 @@ __device__ __forceinline__ bool allreduce_value(const GemvArgs& a, uint32_t e, i
                  (static_cast<int64_t>(par) * a.world + a.rank) * slot_words + off;
     st_volatile_u2(dst, __float_as_uint(part), e);
   }
+}
+
+__device__ __forceinline__ bool ar_poll(const GemvArgs& a, uint32_t e, int64_t row, int b,
+                                        uint64_t t0, float& sum) {
+  const int par = static_cast<int>(e & 1u);
+  const int64_t slot_words = a.n * a.batch;
+  const int64_t off = row * a.batch + b;
   const uint2* own = reinterpret_cast<const uint2*>(a.bufs[a.rank] + kArHeaderBytes) +
                      static_cast<int64_t>(par) * a.world * slot_words + off;
   uint2 w[kArMaxRanks];
-  const uint64_t t0 = gemv_timer_ns();
   for (int spin = 0;; ++spin) {
     bool ready = true;
 #pragma unroll
@@ -163,6 +171,24 @@ __device__ __forceinline__ bool allreduce_value(const GemvArgs& a, uint32_t e, i
   for (int p = 0; p < kArMaxRanks; ++p)
     if (p < a.world) sum += __uint_as_float(w[p].x);
   return true;
+}
+
+// Epilogue of one output value: projection rounding, SwiGLU, residual, store.
+template <typename T, bool GLU>
+__device__ __forceinline__ void emit_value(const GemvArgs& a, int64_t row, int b, float dot,
+                                           float dot2) {
+  float v = round_to<T>(dot);  // projection output in the model dtype
+  if (GLU) {
+    const float up = round_to<T>(dot2);
+    const float sg = round_to<T>(v / (1.f + expf(-v)));  // act_fn(gate)
+    v = round_to<T>(sg * up);
+  }
+  if (a.residual != nullptr)
+    v = round_to<T>(to_float<T>(static_cast<const T*>(a.residual)[b * a.res_stride + row]) + v);
+  if (a.y_fp32)
+    static_cast<float*>(a.y)[b * a.y_stride + row] = v;
+  else
+    static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
 }
 
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t bytes) {
@@ -382,27 +408,10 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
           const int64_t row = rb + gq + (e >> 1) * 8;
           const int b = nt * 8 + 2 * tq + (e & 1);
           if (b >= a.batch || row >= a.n) continue;
-          float dot = acc[nt][e];
-          if (AR) {  // sum the ranks' partial dot products before rounding
-            float sum = 0.f;
-            if (!allreduce_value(a, s_epoch, row, b, dot, sum)) {
-              atomicExch(&s_ar_ok, 0);
-              continue;
-            }
-            dot = sum;
-          }
-          float v = round_to<T>(dot);  // projection output in the model dtype
-          if (GLU) {
-            const float up = round_to<T>(acc2[nt][e]);
-            const float sg = round_to<T>(v / (1.f + expf(-v)));  // act_fn(gate)
-            v = round_to<T>(sg * up);
-          }
-          if (a.residual != nullptr)
-            v = round_to<T>(to_float<T>(static_cast<const T*>(a.residual)[b * a.res_stride + row]) + v);
-          if (a.y_fp32)
-            static_cast<float*>(a.y)[b * a.y_stride + row] = v;
+          if (AR)
+            ar_push(a, s_epoch, row, b, acc[nt][e]);  // summed and emitted after the loop
           else
-            static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
+            emit_value<T, GLU>(a, row, b, acc[nt][e], acc2[nt][e]);
         }
     }
 #pragma unroll
@@ -411,6 +420,26 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
       for (int e = 0; e < 4; ++e) acc[nt][e] = acc2[nt][e] = 0.f;
   }
   cp_async_wait<0>();
+  if (AR && ws == 0) {  // every partial of this CTA is out: sum the ranks', emit
+    const uint64_t t0 = gemv_timer_ns();
+    for (int g2 = 0; g2 < n_groups; ++g2) {
+      const int64_t rb2 = first + g2 * gstride + wrow * 16;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int64_t row = rb2 + gq + (e >> 1) * 8;
+          const int b = nt * 8 + 2 * tq + (e & 1);
+          if (b >= a.batch || row >= a.n) continue;
+          float sum = 0.f;
+          if (!ar_poll(a, s_epoch, row, b, t0, sum)) {
+            atomicExch(&s_ar_ok, 0);
+            continue;
+          }
+          emit_value<T, GLU>(a, row, b, sum, 0.f);
+        }
+    }
+  }
   if (AR) {
     __syncthreads();
     if (threadIdx.x == 0 && s_ar_ok) reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] = s_epoch;
@@ -596,33 +625,29 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         if (lane != b || b >= a.batch) continue;
-        float dot = acc[b];
-        if (AR) {
-          float sum = 0.f;
-          if (!allreduce_value(a, s_epoch, row, b, dot, sum)) {
-            atomicExch(&s_ar_ok, 0);
-            continue;
-          }
-          dot = sum;
-        }
-        float v = round_to<T>(dot);
-        if (GLU) {
-          const float up = round_to<T>(acc2[b]);
-          const float sg = round_to<T>(v / (1.f + expf(-v)));
-          v = round_to<T>(sg * up);
-        }
-        if (a.residual != nullptr)
-          v = round_to<T>(to_float<T>(static_cast<const T*>(a.residual)[b * a.res_stride + row]) + v);
-        if (a.y_fp32)
-          static_cast<float*>(a.y)[b * a.y_stride + row] = v;
+        if (AR)
+          ar_push(a, s_epoch, row, b, acc[b]);  // summed and emitted after the loop
         else
-          static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
+          emit_value<T, GLU>(a, row, b, acc[b], acc2[b]);
       }
     }
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
   }
   cp_async_wait<0>();
+  if (AR && ws == 0 && lane < a.batch) {  // every partial is out: sum the ranks', emit
+    const uint64_t t0 = gemv_timer_ns();
+    for (int g2 = 0; g2 < n_groups; ++g2) {
+      const int64_t row = first + g2 * gstride + wrow;
+      if (row >= a.n) continue;
+      float sum = 0.f;
+      if (!ar_poll(a, s_epoch, row, lane, t0, sum)) {
+        atomicExch(&s_ar_ok, 0);
+        break;
+      }
+      emit_value<T, GLU>(a, row, lane, sum, 0.f);
+    }
+  }
   if (AR) {
     __syncthreads();
     if (threadIdx.x == 0 && s_ar_ok) reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] = s_epoch;
