@@ -491,6 +491,12 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
         if world > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms, e2e_ms = float(t[0]), float(t[1])
+        if args.profile_step:   # one eager step for `ncu --profile-from-start off`
+            torch.cuda.synchronize(dev)
+            torch.cuda.profiler.start()
+            tp.step()
+            torch.cuda.synchronize(dev)
+            torch.cuda.profiler.stop()
         status = _capi.device_status(dev)
         # bytes this rank reads per step: its weight shard + its KV heads at the mean context
         wbytes = sum(x.numel() for lw in shard.layers for x in
@@ -534,6 +540,77 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
             "gpu_launches": (7 * len(shard.layers) + 1) * K,
             "clocks": clocks.summary()}
     print(json.dumps(line), flush=True)
+
+
+GEMV_SHAPES = {  # one Qwen3-14B layer at batch 1: (rows, input width, SwiGLU)
+    "qkv": (7168, 5120, False), "o": (5120, 5120, False), "gateup": (17408, 5120, True),
+    "down": (5120, 17408, False),
+}
+
+
+def run_gemv(args, rank: int, world: int, dev: torch.device):
+    """Weight-streaming rate of helm_decode_gemv on the projection shapes of one
+    Qwen3-14B layer (batch 1; RMSNorm fused on q/k/v and gate/up).  Each shape
+    runs as CUDA graphs of 20 calls; value = weight bytes / time over all of
+    them.  --gemv-shape restricts the run to one shape (eager calls only), the
+    form used for an ncu capture."""
+    from helm_b200 import _capi
+    shapes = [args.gemv_shape] if args.gemv_shape else list(GEMV_SHAPES)
+    per, tot_bytes, tot_us = {}, 0, 0.0
+    for name in shapes:
+        N, K, glu = GEMV_SHAPES[name]
+        g = torch.Generator(device=dev).manual_seed(0)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        w2 = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16) if glu else None
+        x = torch.randn(1, K, device=dev, generator=g).to(torch.bfloat16)
+        nw = torch.ones(K, device=dev, dtype=torch.bfloat16) if name in ("qkv", "gateup") else None
+        y = torch.empty(1, N, device=dev, dtype=torch.bfloat16)
+        fn = lambda: _capi.decode_gemv(x, w, out=y, norm_w=nw, w2=w2)  # noqa: E731
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        if args.gemv_shape:
+            for _ in range(args.steps):
+                fn()
+            torch.cuda.synchronize(dev)
+            continue
+        gr = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.cuda.graph(gr, stream=side):
+            for _ in range(20):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        gr.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(1, args.steps // 20)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / (20 * reps)
+        nbytes = N * K * 2 * (2 if glu else 1)
+        per[name] = {"rows": N, "k": K, "swiglu": glu, "us": us, "gbs": nbytes / us / 1e3}
+        tot_bytes += nbytes
+        tot_us += us
+        del w, w2
+    if rank != 0 or args.gemv_shape:
+        return
+    hbm, peak_src = _peaks()
+    value = tot_bytes / tot_us / 1e3
+    print(json.dumps({"metric": "decode GEMV weight-streaming rate (Qwen3-14B layer, batch 1)",
+                      "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+                      "warmup": args.warmup, "ms_per_step": tot_us / 1e3,
+                      "higher_is_better": True, "scaling": "none", "vs_baseline": None,
+                      "dtype": "bf16", "data": "synthetic",
+                      "config": {"workload": "gemv: the four projections of one Qwen3-14B layer",
+                                 "shapes": per},
+                      "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s",
+                                   "frac": value / hbm, "traffic": None,
+                                   "peak_source": peak_src},
+                      "gpu_launches": 20 * max(1, args.steps // 20) * len(per)}), flush=True)
 
 
 def _h2d_gbs(dev: torch.device, nbytes: int = 1 << 30) -> float:
@@ -661,12 +738,17 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["config2", "seqsplit128k"] + sorted(MODEL_WORKLOADS)
-                    + sorted(TP_WORKLOADS),
+    ap.add_argument("--workload", choices=["config2", "seqsplit128k", "gemv"]
+                    + sorted(MODEL_WORKLOADS) + sorted(TP_WORKLOADS),
                     default="config2",
                     help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
                          "configs[3] split across the GPUs (strong scaling); or whole-model "
                          "decode tok/s of configs[0] (config1) / configs[2] (config3)")
+    ap.add_argument("--gemv-shape", choices=sorted(GEMV_SHAPES), default=None,
+                    help="gemv workload: run one shape with eager calls (for an ncu capture)")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="config4/config5: also run one eager step between "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--stage", choices=["fused", "hf"], default="fused",
                     help="config1/config3: decode step as FusedDecodeStage or as HF modules")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
@@ -700,6 +782,8 @@ def main():
             run_model(args, rank, world, dev)
         elif args.workload in TP_WORKLOADS:
             run_tp(args, rank, world, dev)
+        elif args.workload == "gemv":
+            run_gemv(args, rank, world, dev)
         else:
             run_b200(args, rank, world, dev)
     finally:
