@@ -200,9 +200,43 @@ def _append_prefill_batched(kvcms, k, v, layer_idx: int) -> list:
     return past_lengths
 
 
+def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
+                         attention_mask: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+    """A prefill chunk over the cached pages (the chunk's own rows included)
+    when every item's pages are full, device-resident slots of the pool: K/V
+    gathered to dense [B, Hkv, T, D] by one gather_kv launch, then one
+    attention over them with HELM's chunk-causal (+ padding) mask.  None when
+    the page lists are ragged or partly on the host (the caller falls back)."""
+    dev = q.device
+    pool = _device_pool(kvcms, dev)
+    t = _layer_tables(kvcms, layer_idx, pool)
+    if t is None or t.ragged or t.cold:
+        return None
+    lens = t.used.sum(axis=1).astype(np.int32)
+    T = int(lens.max()) if lens.size else 0
+    if T == 0:
+        return None
+    slots = torch.from_numpy(np.ascontiguousarray(t.slots)).pin_memory().to(dev, non_blocking=True)
+    kl = torch.from_numpy(lens).pin_memory().to(dev, non_blocking=True)
+    k, v = _capi.gather_kv(pool.storage, slots, kl, T, num_kv_heads=pool.shape_tail[1],
+                           page_size=kvcms[0].allocator.page_size)
+    if k.dtype != q.dtype:
+        k, v = k.to(q.dtype), v.to(q.dtype)
+    mask = None
+    if attention_mask is not None:
+        mask = attention_mask[..., :T].to(device=dev, dtype=q.dtype)
+    return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=scale,
+                                          enable_gqa=q.shape[1] != k.shape[1])
+
+
 def _stream_prefill_batched(kvcms, q, layer_idx: int, scale: float,
                             attention_mask: Optional[torch.Tensor] = None,
                             softcap: Optional[float] = None):
+    """Prefill chunk attending over all cached pages (kv_offload.py:203-227)."""
+    if softcap is None and q.device.type == "cuda":
+        out = _prefill_dense_pages(kvcms, q, layer_idx, scale, attention_mask)
+        if out is not None:
+            return out
     lists = [[p for p in kvcms[i].iterate_layer_pages(layer_idx)
               if p.used_tokens > 0 and p.state != "DEAD"] for i in range(q.shape[0])]
     return _prefill_over_pages(q, lists, scale, attention_mask, softcap)

@@ -230,3 +230,32 @@ def test_cpu_pages_made_by_hand_with_cuda_query(dev):
     assert s["prefetch_calls"] == 1 and s["pages_prefetched"] == 1 and s["bytes_prefetched"] > 0
     _close(out, _eager(q, torch.cat([K1, K2.to(dev)], 2), torch.cat([V1, V2.to(dev)], 2)),
            torch.bfloat16)
+
+
+def test_dense_prefill_path_matches_page_walk(dev):
+    """A 64-token prefill chunk over 320 cached tokens: the gather + attention
+    fast path equals the fp32 page walk within the bf16 tolerance, with HELM's
+    chunk-causal mask; with host-resident pages it declines (page walk used)."""
+    from helm_b200.runtime.kv_cache import _prefill_over_pages
+    from helm_b200.runtime.kv_offload import _prefill_dense_pages
+    torch.manual_seed(11)
+    H, D, P, T, S = 2, 64, 16, 320, 64
+    for watermark, expect_fast in ((10 ** 12, True), (2 * 2 * H * P * D * 2, False)):
+        alloc = KVAllocator(1, H, D, page_size=P, dtype=torch.bfloat16)
+        mgr = KVCacheManager(alloc, gpu_high_watermark_bytes=watermark)
+        k = torch.randn(1, H, T, D).to(torch.bfloat16).to(dev)
+        v = torch.randn(1, H, T, D).to(torch.bfloat16).to(dev)
+        mgr.append_prefill(0, k, v)
+        q = torch.randn(1, 4 * H, S, D).to(torch.bfloat16).to(dev)
+        past = T - S
+        i = torch.arange(S, device=dev).view(S, 1)
+        j = torch.arange(T, device=dev).view(1, T)
+        mask = torch.where(j <= past + i, 0.0, torch.finfo(torch.bfloat16).min)
+        mask = mask.to(torch.bfloat16).view(1, 1, S, T)
+        fast = _prefill_dense_pages([mgr], q, 0, D ** -0.5, mask)
+        ref = _prefill_over_pages(q, [mgr.iterate_layer_pages(0)], D ** -0.5, mask, None)
+        if expect_fast:
+            assert fast is not None
+            _close(fast, ref, torch.bfloat16)
+        else:
+            assert fast is None
