@@ -23,7 +23,6 @@ multi-GPU form of the decode hot path, without the single-GPU offload policy.
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 from typing import List, Optional
 
