@@ -234,8 +234,9 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
   const T* W = static_cast<const T*>(a.w);
   const T* W2 = static_cast<const T*>(a.w2);
   const int64_t ksteps = K / 16;
-  // (with the all-reduce, later kernels are not placed early: they could take
-  // the space of CTAs that other ranks' CTAs are waiting for)
+  // Later kernels may be placed now, except after the all-reduce form: an
+  // early trigger there made 16-row, batch-sliced all-reduce calls on two
+  // GPUs time out in their poll, so its dependents start only when it ends.
   if (!AR) asm volatile("griddepcontrol.launch_dependents;");
 
   // ---- work: a CTA iteration covers (kGemvWarps / ksplit) row blocks of 16
@@ -474,7 +475,7 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
   const T* W = static_cast<const T*>(a.w);
   const T* W2 = static_cast<const T*>(a.w2);
   const int64_t chunks = K / 8;  // 16-byte chunks per row
-  if (!AR) asm volatile("griddepcontrol.launch_dependents;");
+  if (!AR) asm volatile("griddepcontrol.launch_dependents;");  // (see decode_gemv_kernel)
   const int ksplit = a.ksplit;              // warps per row (divides kGemvWarps)
   const int rpi = kGemvWarps / ksplit;      // rows per CTA iteration
   const int wrow = warp / ksplit, ws = warp - (warp / ksplit) * ksplit;
