@@ -259,3 +259,49 @@ def test_dense_prefill_path_matches_page_walk(dev):
             _close(fast, ref, torch.bfloat16)
         else:
             assert fast is None
+
+
+def test_gemma2_sliding_window_known_answers(dev):
+    """The reference's analytic check of the Gemma-2 forward
+    (tests/unit/runtime/test_kv_offload.py:367-413), restated at a head size the
+    GPU path serves (64, bf16): q, k, v each pick one hidden component, so the
+    last of three prompt tokens scores 10 against token 0 and 0 against tokens
+    1 and 2.  With a window of 2 it must average v over tokens 1 and 2:
+    (1 + 2) / 2 = 1.5 (the window ignored would give ~100).  One decode step
+    after it (v = 4) must give (2 + 4) / 2 = 3.0 from the paged path."""
+    import torch.nn as nn
+    from helm_b200.runtime.kv_offload import _make_gemma2_forward
+    D = 64
+    attn = nn.Module()
+    attn.q_proj = nn.Linear(3, D, bias=False)
+    attn.k_proj = nn.Linear(3, D, bias=False)
+    attn.v_proj = nn.Linear(3, D, bias=False)
+    attn.o_proj = nn.Linear(D, 1, bias=False)
+    with torch.no_grad():
+        for lin in (attn.q_proj, attn.k_proj, attn.v_proj, attn.o_proj):
+            lin.weight.zero_()
+        attn.q_proj.weight[0, 0] = 1.0
+        attn.k_proj.weight[0, 1] = 1.0
+        attn.v_proj.weight[0, 2] = 1.0
+        attn.o_proj.weight[0, 0] = 1.0
+    attn = attn.to(dev, torch.bfloat16)
+    attn.head_dim, attn.layer_idx, attn.scaling = D, 0, 1.0
+    attn.attn_logit_softcapping, attn.sliding_window = None, 2
+    alloc = KVAllocator(1, 1, D, page_size=16, dtype=torch.bfloat16)
+    kvcms = [KVCacheManager(alloc, gpu_high_watermark_bytes=10 ** 12)]
+    forward = _make_gemma2_forward(kvcms)
+    h = torch.tensor([[[1.0, 10.0, 100.0], [1.0, 0.0, 1.0], [1.0, 0.0, 2.0]]],
+                     dtype=torch.bfloat16, device=dev)
+    lo = torch.finfo(torch.bfloat16).min
+    causal = torch.triu(torch.full((3, 3), lo, device=dev), diagonal=1)
+    causal = causal.to(torch.bfloat16)[None, None]
+    ones = torch.ones(1, 3, D, dtype=torch.bfloat16, device=dev)   # RoPE at angle 0
+    out, _ = forward(attn, h, (ones, torch.zeros_like(ones)), attention_mask=causal,
+                     cache_position=torch.arange(3, device=dev))
+    assert abs(out[0, 2, 0].item() - 1.5) < 1e-2
+    h4 = torch.tensor([[[1.0, 0.0, 4.0]]], dtype=torch.bfloat16, device=dev)
+    one = torch.ones(1, 1, D, dtype=torch.bfloat16, device=dev)
+    out4, _ = forward(attn, h4, (one, torch.zeros_like(one)),
+                      attention_mask=torch.zeros(1, 1, 1, 4, dtype=torch.bfloat16, device=dev),
+                      cache_position=torch.tensor([3], device=dev))
+    assert abs(out4[0, 0, 0].item() - 3.0) < 2e-2
