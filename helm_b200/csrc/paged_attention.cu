@@ -559,12 +559,16 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
     const int worker_len = max(0, min(W, total - worker_first));
     const int64_t kv_rows = static_cast<int64_t>(a.hkv) * a.page_size;
 
-    auto rows_of = [&](int s, int& row_k, bool& ok) {
+    // row_k: pool row of the tile's K; tail: the tile is in its sequence's last
+    // page (the one a preceding append kernel may still be writing)
+    auto rows_of = [&](int s, int& row_k, bool& ok, bool& tail) {
       ok = s < worker_len;
       row_k = 0;
+      tail = false;
       if (!ok) return;
       const TilePos p = locate(s_cum, a.batch, a.hkv, worker_first + s);
       const int page = p.t / a.tiles_per_page;
+      tail = page == (s_cum[p.b + 1] - s_cum[p.b]) / a.tiles_per_page - 1;
       const int row_off = (p.t - page * a.tiles_per_page) * kTileRows;
       int slot = a.page_table[static_cast<int64_t>(p.b) * a.pt_sb + page];
       if (slot < 0 || slot >= a.pool_pages) {
@@ -575,15 +579,42 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
                                row_off);
     };
 
+    auto issue_tile = [&](int buf, int row_k) {
+      uint8_t* kdst = smem + buf * kStageBytes + w * 2 * kTileBytes;
+      uint8_t* vdst = kdst + kTileBytes;
+      const int row_v = static_cast<int>(row_k + kv_rows);
+#pragma unroll
+      for (int hb = 0; hb < kBoxes; ++hb) {
+        tma_load_2d(kdst + hb * 2048, &tmap, hb * 64, row_k, &full[buf]);
+        tma_load_2d(vdst + hb * 2048, &tmap, hb * 64, row_v, &full[buf]);
+      }
+    };
+
     int row_cur, row_nxt;
-    bool ok_cur, ok_nxt;
-    rows_of(j, row_cur, ok_cur);
+    bool ok_cur, ok_nxt, tail_cur, tail_nxt;
+    rows_of(j, row_cur, ok_cur, tail_cur);
+    // The first `pre` stages (free ring slots) are posted before waiting for the
+    // kernel before this one: their transaction counts, and the TMA loads of
+    // tiles outside their sequence's last page (with decode overlap the only
+    // page that kernel may write); last-page tiles are loaded after the wait.
+    const int pre = min(min(NS, kWin), n_stages);
+    for (int jj = 0; jj < pre; ++jj) {
+      const bool mine = (j == jj) && ok_cur;
+      const unsigned issuing = __ballot_sync(0xffffffffu, mine);
+      if (lane == 0) mbar_arrive_expect_tx(&full[jj], __popc(issuing) * 2 * kTileBytes);
+      __syncwarp();
+      if (mine && !tail_cur) issue_tile(jj, row_cur);
+    }
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int win = 0; win * kWin < n_stages; ++win) {
-      rows_of((win + 1) * kWin + j, row_nxt, ok_nxt);  // next window's page-table reads
+      rows_of((win + 1) * kWin + j, row_nxt, ok_nxt, tail_nxt);  // next window's page table
       for (int jj = 0; jj < kWin; ++jj) {
         const int s = win * kWin + jj;
         if (s >= n_stages) break;
+        if (s < pre) {  // posted above; its last-page tiles go now
+          if (j == jj && ok_cur && tail_cur) issue_tile(s, row_cur);
+          continue;
+        }
         const int buf = s % NS, n = s / NS;
         int alive = 1;
         if (lane == 0 && n > 0) alive = mbar_wait(&empty[buf], (n - 1) & 1) ? 1 : 0;
@@ -593,19 +624,11 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
         const unsigned issuing = __ballot_sync(0xffffffffu, mine);
         if (lane == 0) mbar_arrive_expect_tx(&full[buf], __popc(issuing) * 2 * kTileBytes);
         __syncwarp();
-        if (mine) {
-          uint8_t* kdst = smem + buf * kStageBytes + w * 2 * kTileBytes;
-          uint8_t* vdst = kdst + kTileBytes;
-          const int row_v = static_cast<int>(row_cur + kv_rows);
-#pragma unroll
-          for (int hb = 0; hb < kBoxes; ++hb) {
-            tma_load_2d(kdst + hb * 2048, &tmap, hb * 64, row_cur, &full[buf]);
-            tma_load_2d(vdst + hb * 2048, &tmap, hb * 64, row_v, &full[buf]);
-          }
-        }
+        if (mine) issue_tile(buf, row_cur);
       }
       row_cur = row_nxt;
       ok_cur = ok_nxt;
+      tail_cur = tail_nxt;
     }
     return;
   }

@@ -118,12 +118,14 @@ int helm_paged_decode_attention(const void* q, int64_t q_stride_b, int64_t q_str
  * the previous setting).  When on, helm_paged_decode_attention and
  * helm_paged_decode_attention_noalloc launch the decode kernel as a
  * programmatic dependent of the kernel before it on the stream (PDL): the
- * kernel is placed while that one still runs and reads kv_lens, num_pages and
- * page_table early, but waits for it to finish before it reads q, the pool or
- * the mask and before it writes anything.  Turn it on only where the kernel
+ * kernel is placed while that one still runs, reads kv_lens, num_pages and
+ * page_table and starts loading K/V tiles outside each sequence's last page
+ * early, but waits for it to finish before it reads q, the mask or a last
+ * page, and before it writes anything.  Turn it on only where the kernel
  * immediately before each call does not write kv_lens, num_pages, page_used,
- * page_start or page_table (for example when they were uploaded by an earlier
- * copy, as in a captured decode step).  No counterpart in the reference.
+ * page_start or page_table, and writes no K/V page other than the sequences'
+ * last pages (for example the fused append of the new token in a captured
+ * decode step).  No counterpart in the reference.
  */
 int helm_set_decode_overlap(int enable);
 
