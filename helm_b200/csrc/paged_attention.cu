@@ -722,23 +722,25 @@ __global__ void __launch_bounds__(Layout<D>::kThreads, 1)
 }
 
 // Merges the pairs whose tiles were split across CTAs (second kernel of a
-// call).  CTA (pair p, chunk) owns 32 float4 elements of p's G x D output
-// block, one per lane.  Its sources are the CTA partials of CTAs
+// call).  CTA (pair p, chunk) owns 16 float4 elements of p's G x D output
+// block; each half-warp covers those 16 elements for one group of sources.  Its sources are the CTA partials of CTAs
 // vf/NCW .. vl_end/NCW (slots c + p) and, when the pair's last worker
 // continues into the next pair, that worker's partial (slot vl + p).  The
-// kMergeWarps warps take disjoint subsets of the sources (loads of up to
-// kMergeBatch sources in flight per lane, a running rescaled state between
+// kMergeGroups half-warps take disjoint subsets of the sources (loads of up
+// to kMergeBatch sources in flight per lane, a running rescaled state between
 // batches); their states meet in shared memory.  With few long sequences a
-// pair has dozens of sources, so spreading them over warps keeps the merge at
-// one or two L2 round trips.
+// pair has up to ~150 sources (one per CTA), so spreading them over 16 groups
+// keeps the merge at one or two L2 round trips.
 constexpr int kMergeWarps = 8;
 constexpr int kMergeThreads = kMergeWarps * 32;
-constexpr int kMergeBatch = 8;
+constexpr int kMergeGroups = kMergeWarps * 2;
+constexpr int kMergeElems = 16;  // float4 elements per CTA
+constexpr int kMergeBatch = 6;
 
 template <typename T, int D, int NCW>
 __global__ void __launch_bounds__(kMergeThreads, 4) merge_split_pairs_kernel(const DecodeArgs a) {
   extern __shared__ int s_cum_m[];
-  __shared__ float s_st[kMergeWarps][6][32];  // per warp: M, L, acc.xyzw per lane
+  __shared__ float s_st[kMergeGroups][6][kMergeElems];  // per group: M, L, acc.xyzw
   asm volatile("griddepcontrol.launch_dependents;");
   const int p = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -757,18 +759,20 @@ __global__ void __launch_bounds__(kMergeThreads, 4) merge_split_pairs_kernel(con
   const int K = n_cta + (ps.last_continues ? 1 : 0);
   const int G = a.group;
   constexpr int D4 = D / 4;
-  const int e = blockIdx.y * 32 + lane;
+  const int el = lane & (kMergeElems - 1);
+  const int grp = warp * 2 + (lane >> 4);  // source group of this half-warp
+  const int e = blockIdx.y * kMergeElems + el;
   const bool active = e < G * D4;
   const int hg = active ? e / D4 : 0, d4 = active ? e - (e / D4) * D4 : 0;
   float M = -INFINITY, Lsum = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  // warp w: sources w, w + kMergeWarps, ...
-  for (int k0 = warp; active && k0 < K; k0 += kMergeWarps * kMergeBatch) {
+  // group q: sources q, q + kMergeGroups, ...
+  for (int k0 = grp; active && k0 < K; k0 += kMergeGroups * kMergeBatch) {
     float2 ml[kMergeBatch];
     float4 o[kMergeBatch];
 #pragma unroll
     for (int i = 0; i < kMergeBatch; ++i) {  // issue the whole batch first
-      const int k = k0 + i * kMergeWarps;
+      const int k = k0 + i * kMergeGroups;
       ml[i] = make_float2(-INFINITY, 0.f);
       o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k < K) {
@@ -802,27 +806,27 @@ __global__ void __launch_bounds__(kMergeThreads, 4) merge_split_pairs_kernel(con
     }
     M = Mb;
   }
-  s_st[warp][0][lane] = M;
-  s_st[warp][1][lane] = Lsum;
-  s_st[warp][2][lane] = acc.x;
-  s_st[warp][3][lane] = acc.y;
-  s_st[warp][4][lane] = acc.z;
-  s_st[warp][5][lane] = acc.w;
+  s_st[grp][0][el] = M;
+  s_st[grp][1][el] = Lsum;
+  s_st[grp][2][el] = acc.x;
+  s_st[grp][3][el] = acc.y;
+  s_st[grp][4][el] = acc.z;
+  s_st[grp][5][el] = acc.w;
   __syncthreads();
-  if (warp != 0 || !active) return;
+  if (threadIdx.x >= kMergeElems || !active) return;
   float Mt = -INFINITY;
 #pragma unroll
-  for (int w = 0; w < kMergeWarps; ++w) Mt = fmaxf(Mt, s_st[w][0][lane]);
+  for (int q = 0; q < kMergeGroups; ++q) Mt = fmaxf(Mt, s_st[q][0][el]);
   const float m_use = Mt == -INFINITY ? 0.f : Mt;
   float L = 0.f, ox = 0.f, oy = 0.f, oz = 0.f, ow = 0.f;
 #pragma unroll
-  for (int w = 0; w < kMergeWarps; ++w) {
-    const float f = exp2f(s_st[w][0][lane] - m_use);  // 0 for warps without sources
-    L += s_st[w][1][lane] * f;
-    ox += s_st[w][2][lane] * f;
-    oy += s_st[w][3][lane] * f;
-    oz += s_st[w][4][lane] * f;
-    ow += s_st[w][5][lane] * f;
+  for (int q = 0; q < kMergeGroups; ++q) {
+    const float f = exp2f(s_st[q][0][el] - m_use);  // 0 for groups without sources
+    L += s_st[q][1][el] * f;
+    ox += s_st[q][2][el] * f;
+    oy += s_st[q][3][el] * f;
+    oz += s_st[q][4][el] * f;
+    ow += s_st[q][5][el] * f;
   }
   const int b = p / a.hkv, h = p - (p / a.hkv) * a.hkv;
   const float inv = 1.f / fmaxf(L, 1e-12f);
@@ -904,7 +908,7 @@ int launch(const DecodeArgs& a, const void* pool, int64_t pool_rows, int grid,
   // merge of split pairs: a programmatic dependent of the decode kernel
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(a.batch * a.hkv),
-                     static_cast<unsigned>((a.group * (D / 4) + 31) / 32));
+                     static_cast<unsigned>((a.group * (D / 4) + kMergeElems - 1) / kMergeElems));
   cfg.blockDim = dim3(kMergeThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(a.batch + 1) * sizeof(int);
   cfg.stream = stream;
