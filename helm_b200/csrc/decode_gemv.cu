@@ -636,17 +636,21 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
     for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
   }
   cp_async_wait<0>();
-  if (AR && ws == 0 && lane < a.batch) {  // every partial is out: sum the ranks', emit
+  if (AR && ws == 0) {  // every partial is out: sum the ranks', emit
+    // the warp's (row group, batch row) values spread over its lanes, so the
+    // polls of different rows run concurrently
     const uint64_t t0 = gemv_timer_ns();
-    for (int g2 = 0; g2 < n_groups; ++g2) {
+    const int items = n_groups * a.batch;
+    for (int it = lane; it < items; it += 32) {
+      const int g2 = it / a.batch, b = it - (it / a.batch) * a.batch;
       const int64_t row = first + g2 * gstride + wrow;
       if (row >= a.n) continue;
       float sum = 0.f;
-      if (!ar_poll(a, s_epoch, row, lane, t0, sum)) {
+      if (!ar_poll(a, s_epoch, row, b, t0, sum)) {
         atomicExch(&s_ar_ok, 0);
         break;
       }
-      emit_value<T, GLU>(a, row, lane, sum, 0.f);
+      emit_value<T, GLU>(a, row, b, sum, 0.f);
     }
   }
   if (AR) {
