@@ -613,6 +613,87 @@ def run_gemv(args, rank: int, world: int, dev: torch.device):
                       "gpu_launches": 20 * max(1, args.steps // 20) * len(per)}), flush=True)
 
 
+PREFILL = dict(Hq=40, Hkv=8, D=128, P=64, S=512)  # configs[3] (Qwen3-14B), one 512-token chunk
+
+
+def run_prefill(args, rank: int, world: int, dev: torch.device):
+    """Chunk-prefill attention of configs[3]: one layer's 512-query chunk over
+    --seq-len cached tokens (default 131072, the prompt's last chunk), HELM's
+    chunk-causal mask in bf16.  Times helm_paged_prefill_attention (pages read
+    in place) and, beside it, the path it replaces: gather_kv to dense K/V +
+    torch SDPA with the mask.  value = attention TFLOP/s of the native kernel
+    (4 * S * Hq * T * D per call, every key of every row computed, as the
+    reference's masked branch does)."""
+    import torch.nn.functional as F
+
+    from helm_b200 import _capi
+    c = PREFILL
+    Tk = args.seq_len if args.seq_len_given else 131072
+    S, Hq, Hkv, D, Pg = c["S"], c["Hq"], c["Hkv"], c["D"], c["P"]
+    pages = Tk // Pg
+    g = torch.Generator(device=dev).manual_seed(0)
+    pool = torch.randn(pages + 8, 2, Hkv, Pg, D, device=dev, generator=g).to(torch.bfloat16)
+    table = torch.randperm(pages + 8, device=dev, generator=g)[:pages].view(1, pages).to(torch.int32)
+    lens = torch.tensor([Tk], dtype=torch.int32, device=dev)
+    q = torch.randn(1, S, Hq, D, device=dev, generator=g).to(torch.bfloat16).transpose(1, 2)
+    past = Tk - S
+    i = torch.arange(S, device=dev).view(S, 1)
+    j = torch.arange(Tk, device=dev).view(1, Tk)
+    mask = torch.where(j <= past + i, 0.0, torch.finfo(torch.bfloat16).min)
+    mask = mask.to(torch.bfloat16).view(1, 1, S, Tk)
+    scale = D ** -0.5
+
+    def native():
+        return _capi.paged_prefill_attention(q, pool, table, lens, num_kv_heads=Hkv, page_size=Pg,
+                                             scale=scale, max_kv_len=Tk, mask=mask)
+
+    def gathered():
+        k, v = _capi.gather_kv(pool, table, lens, Tk, num_kv_heads=Hkv, page_size=Pg)
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=scale,
+                                              enable_gqa=True)
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    steps = args.steps if args.steps_given else 10
+    a = native().float()
+    b = gathered().float()
+    diff = float((a - b).abs().max())
+    ms = timed(native, steps)
+    ms_ref = timed(gathered, max(1, steps // 2))
+    if rank != 0:
+        return
+    flop = 4.0 * S * Hq * Tk * D
+    tflops = flop / (ms * 1e-3) / 1e12
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            peak, src = float(json.load(f)["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops)"
+    except (OSError, KeyError, ValueError):
+        peak, src = 1590.0, "fallback 1.59 PFLOP/s"
+    print(json.dumps({"metric": "chunk-prefill attention TFLOP/s (configs[3] chunk, one layer)",
+                      "value": tflops, "unit": "TFLOP/s", "n_gpus": 1, "steps": steps,
+                      "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                      "scaling": "none", "vs_baseline": None, "dtype": "bf16",
+                      "data": "synthetic",
+                      "config": {"workload": f"prefill: 1 x {S} queries x {Hq}/{Hkv} heads over "
+                                             f"{Tk} cached tokens, page {Pg}, HELM chunk mask",
+                                 "gather_sdpa_ms": ms_ref, "speedup_vs_gather_sdpa": ms_ref / ms,
+                                 "max_abs_diff_vs_gather_sdpa": diff},
+                      "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak,
+                                   "unit": "TFLOP/s", "frac": tflops / peak, "traffic": None,
+                                   "peak_source": src},
+                      "gpu_launches": 2 * steps}), flush=True)
+
+
 def _h2d_gbs(dev: torch.device, nbytes: int = 1 << 30) -> float:
     """Pinned host -> device copy bandwidth (best of 5), the link roofline."""
     h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
@@ -738,7 +819,7 @@ def main():
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["config2", "seqsplit128k", "gemv"]
+    ap.add_argument("--workload", choices=["config2", "seqsplit128k", "gemv", "prefill"]
                     + sorted(MODEL_WORKLOADS) + sorted(TP_WORKLOADS),
                     default="config2",
                     help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
@@ -755,11 +836,13 @@ def main():
                     help="seqsplit128k: how partial states cross GPUs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-len", type=int, default=T,
-                    help="tokens per sequence (profiling a smaller case only)")
+                    help="tokens per sequence (profiling a smaller case only; for the "
+                         "prefill workload, the cached tokens, default 131072)")
     ap.add_argument("--pool-pages", type=int, default=POOL,
                     help="page-pool slots (profiling a smaller case only)")
     args = ap.parse_args()
     args.steps_given = args.steps is not None
+    args.seq_len_given = args.seq_len != T
     if args.steps is None:
         args.steps = 50
     _set_shape(args.seq_len, args.pool_pages)
@@ -784,6 +867,8 @@ def main():
             run_tp(args, rank, world, dev)
         elif args.workload == "gemv":
             run_gemv(args, rank, world, dev)
+        elif args.workload == "prefill":
+            run_prefill(args, rank, world, dev)
         else:
             run_b200(args, rank, world, dev)
     finally:

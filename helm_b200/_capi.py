@@ -55,6 +55,17 @@ _SIGNATURES = {
         _I, _I, _I, _I, _I, _I, _P]),
     "helm_copy_pages": (_I, [_P, _P, _I64, _P, _P, _I64, _P]),
     "helm_gather_kv": (_I, [_P, _I64, _P, _I64, _I, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P]),
+    "helm_paged_prefill_workspace_bytes": (_I64, [_I, _I, _I, _I, _I, _I, _I]),
+    "helm_paged_prefill_attention": (_I, [
+        _P, _I64, _I64, _I64,      # q, strides (b, h, s)
+        _P, _I64,                  # pool, pool_pages
+        _P, _I64, _I,              # page_table, pt_stride_b, max_pages
+        _P,                        # kv_lens
+        _P, _I, _I64, _I64,        # mask, mask_dtype, mask strides (b, q)
+        _P, _I64, _I64, _I64,      # out, strides (b, h, s)
+        _P, _I64,                  # workspace, bytes
+        _I, _I, _I, _I, _I, _I,    # batch, q_len, hq, hkv, head_dim, page_size
+        _I, _I, _F, _F, _I, _P]),  # dtype, causal, scale, softcap, max_kv_len, stream
     "helm_merge_attention_states": (_I, [_P, _I, _I64, _P, _I64, _I, _I64, _I, _P, _I, _P, _P]),
     "helm_decode_gemv": (_I, [_P, _I64, _P, _F, _P, _P, _I64, _I64, _P, _I64, _P, _I64, _I, _I,
                               _I, _P]),
@@ -247,6 +258,70 @@ def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torc
             _stream_handle(dev, stream))
     _check(rc, "helm_paged_decode_attention")
     return out, lse
+
+
+def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torch.Tensor,
+                            kv_lens: torch.Tensor, *, num_kv_heads: int, page_size: int,
+                            scale: float, max_kv_len: int, mask: Optional[torch.Tensor] = None,
+                            causal: bool = False, softcap: Optional[float] = None,
+                            out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
+    """Chunk-prefill attention over a page pool (the chunk's K/V already in it).
+
+    q [B, Hq, S, D] (any strides, unit dim stride); pool [slots, 2, Hkv, P, D];
+    page_table int32 [B, max_pages]; kv_lens int32 [B] (query i of sequence b
+    sits at position kv_lens[b] - S + i); mask additive [B or 1, 1, S, >= T]
+    or None; max_kv_len = max(kv_lens).  Returns out [B, Hq, S, D] in q.dtype,
+    a view of a [B, S, Hq, D] buffer unless `out` is given.
+    """
+    if q.device.type != "cuda":
+        raise HelmError("paged_prefill_attention runs on CUDA tensors only")
+    B, Hq, S, D = q.shape
+    if q.stride(3) != 1:
+        raise HelmError("q must have a unit stride on the head dim")
+    if pool.dtype != q.dtype:
+        raise HelmError(f"KV pool dtype {pool.dtype} != query dtype {q.dtype}")
+    if page_table.dtype != torch.int32 or kv_lens.dtype != torch.int32:
+        raise HelmError("page_table and kv_lens must be int32")
+    if page_table.stride(1) != 1:
+        raise HelmError("page_table rows must be contiguous")
+    dev = q.device
+    if out is None:
+        out = torch.empty(B, S, Hq, D, dtype=q.dtype, device=dev).transpose(1, 2)
+    if out.dtype != q.dtype or out.shape != q.shape or out.stride(3) != 1:
+        raise HelmError("out must be [B, Hq, S, D] in the query dtype, unit dim stride")
+    mask_ptr, mask_dt, mask_sb, mask_sq = None, 0, 0, 0
+    if mask is not None:
+        if mask.dim() != 4 or mask.shape[2] != S or mask.shape[3] < max_kv_len:
+            raise HelmError("mask must be [B or 1, 1, S, >= max_kv_len]")
+        if mask.stride(-1) != 1:
+            mask = mask.contiguous()
+        mask_ptr, mask_dt = mask.data_ptr(), helm_dtype(mask.dtype)
+        mask_sb = mask.stride(0) if mask.shape[0] > 1 else 0
+        mask_sq = mask.stride(2)
+    dt = helm_dtype(q.dtype)
+    with torch.cuda.device(dev):
+        ws_bytes = int(lib().helm_paged_prefill_workspace_bytes(B, S, Hq, num_kv_heads, D, dt,
+                                                                int(max_kv_len)))
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+        rc = lib().helm_paged_prefill_attention(
+            q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
+            pool.data_ptr(), pool.shape[0],
+            page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+            kv_lens.data_ptr(),
+            mask_ptr, mask_dt, mask_sb, mask_sq,
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+            ws.data_ptr(), ws_bytes,
+            B, S, Hq, num_kv_heads, D, page_size, dt, 1 if causal else 0,
+            float(scale), float(softcap or 0.0), int(max_kv_len),
+            _stream_handle(dev, stream))
+    _check(rc, "helm_paged_prefill_attention")
+    return out
+
+
+def prefill_supported(dtype: torch.dtype, head_dim: int, page_size: int) -> bool:
+    """Shapes helm_paged_prefill_attention serves (others return UNSUPPORTED)."""
+    return (dtype in (torch.bfloat16, torch.float16) and head_dim in (64, 128)
+            and page_size % 16 == 0)
 
 
 def kv_append(*, k: torch.Tensor, v: torch.Tensor, pool: Optional[torch.Tensor],

@@ -9,6 +9,7 @@
 #include "kv_ops.cu"
 #include "paged_attention.cu"
 #include "paged_attention_noalloc.cu"
+#include "paged_prefill.cu"
 #include "peer_exchange.cu"
 #include "decode_gemv.cu"
 

@@ -16,6 +16,7 @@ The patched GPU-stage forwards here run, per layer and per decode step:
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from types import MethodType
 from typing import Optional
@@ -201,12 +202,24 @@ def _append_prefill_batched(kvcms, k, v, layer_idx: int) -> list:
 
 
 def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
-                         attention_mask: Optional[torch.Tensor]) -> Optional[torch.Tensor]:
+                         attention_mask: Optional[torch.Tensor],
+                         softcap: Optional[float] = None) -> Optional[torch.Tensor]:
     """A prefill chunk over the cached pages (the chunk's own rows included)
-    when every item's pages are full, device-resident slots of the pool: K/V
-    gathered to dense [B, Hkv, T, D] by one gather_kv launch, then one
-    attention over them with HELM's chunk-causal (+ padding) mask.  None when
-    the page lists are ragged or partly on the host (the caller falls back)."""
+    when every item's pages are full, device-resident slots of the pool.
+
+    Two device paths, both with HELM's additive mask (chunk-causal + padding,
+    kv_offload.py:206-227):
+      * K/V gathered to dense [B, Hkv, T, D] by one gather_kv launch, then one
+        library attention (torch SDPA) over them: the default, ~5x faster than
+        the native kernel at long context on B200 (the library attention runs
+        on the tcgen05 tensor cores; the native kernel on mma.sync);
+      * helm_paged_prefill_attention, reading K/V in place from the pool (no
+        dense copy): used for soft-capped scores, which the library call does
+        not take, and for every chunk when HELM_B200_NATIVE_PREFILL=1.
+    The native kernel needs bf16/fp16, head dim 64 or 128 and a page size that
+    is a multiple of 16.  None when the page lists are ragged or partly on the
+    host, or when a softcap needs the native kernel and the shape is not one
+    of those (the caller walks the pages)."""
     dev = q.device
     pool = _device_pool(kvcms, dev)
     t = _layer_tables(kvcms, layer_idx, pool)
@@ -216,15 +229,27 @@ def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
     T = int(lens.max()) if lens.size else 0
     if T == 0:
         return None
+    P = kvcms[0].allocator.page_size
+    Hkv = pool.shape_tail[1]
     slots = torch.from_numpy(np.ascontiguousarray(t.slots)).pin_memory().to(dev, non_blocking=True)
     kl = torch.from_numpy(lens).pin_memory().to(dev, non_blocking=True)
-    k, v = _capi.gather_kv(pool.storage, slots, kl, T, num_kv_heads=pool.shape_tail[1],
-                           page_size=kvcms[0].allocator.page_size)
+    mask = None if attention_mask is None else attention_mask[..., :T].to(device=dev)
+    native = (pool.storage.dtype == q.dtype and _capi.prefill_supported(q.dtype, q.shape[-1], P)
+              and (mask is None or (mask.dim() == 4 and mask.shape[1] == 1
+                                    and mask.shape[2] == q.shape[2] and mask.shape[3] == T
+                                    and mask.dtype in (torch.float32, torch.bfloat16,
+                                                       torch.float16))))
+    if native and (softcap is not None or os.environ.get("HELM_B200_NATIVE_PREFILL") == "1"):
+        return _capi.paged_prefill_attention(q, pool.storage, slots, kl, num_kv_heads=Hkv,
+                                             page_size=P, scale=scale, max_kv_len=T, mask=mask,
+                                             softcap=softcap)
+    if softcap is not None:
+        return None
+    k, v = _capi.gather_kv(pool.storage, slots, kl, T, num_kv_heads=Hkv, page_size=P)
     if k.dtype != q.dtype:
         k, v = k.to(q.dtype), v.to(q.dtype)
-    mask = None
-    if attention_mask is not None:
-        mask = attention_mask[..., :T].to(device=dev, dtype=q.dtype)
+    if mask is not None:
+        mask = mask.to(dtype=q.dtype)
     return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=scale,
                                           enable_gqa=q.shape[1] != k.shape[1])
 
@@ -233,8 +258,8 @@ def _stream_prefill_batched(kvcms, q, layer_idx: int, scale: float,
                             attention_mask: Optional[torch.Tensor] = None,
                             softcap: Optional[float] = None):
     """Prefill chunk attending over all cached pages (kv_offload.py:203-227)."""
-    if softcap is None and q.device.type == "cuda":
-        out = _prefill_dense_pages(kvcms, q, layer_idx, scale, attention_mask)
+    if q.device.type == "cuda":
+        out = _prefill_dense_pages(kvcms, q, layer_idx, scale, attention_mask, softcap)
         if out is not None:
             return out
     lists = [[p for p in kvcms[i].iterate_layer_pages(layer_idx)

@@ -219,6 +219,50 @@ int helm_gather_kv(const void* kv_pool, int64_t pool_pages, const int32_t* page_
                    int t_max, int dtype, void* stream);
 
 /*
+ * Chunk-prefill attention straight over the page pool: for every sequence b,
+ * the q_len queries of the chunk (already appended: query i sits at position
+ * kv_lens[b] - q_len + i) attend over keys 0 .. kv_lens[b]-1 of the pages in
+ * page_table row b:
+ *     out = softmax(softcap(scale * q K^T) + mask [+ causal limit]) V
+ * fp32 accumulation and softmax state, output in the query dtype.
+ *
+ * Replaces the q_len > 1 branch of perform_streaming_attention
+ * (helm/runtime/kv_cache.py:469-555) as called by _stream_prefill_batched
+ * (helm/runtime/kv_offload.py:206-227).
+ *
+ *  q           [B, Hq, q_len, D] with strides q_stride_b/_h/_s (elements; even)
+ *  kv_pool     [pool_pages, 2, Hkv, page_size, D]; page_size a multiple of 16
+ *  page_table  int32 [B, >= max_pages] (row stride pt_stride_b), kv_lens int32 [B]
+ *  mask        optional additive mask [B or 1, 1, q_len, >= max kv_lens] with
+ *              strides mask_stride_b (0 to broadcast) and mask_stride_q, last
+ *              stride 1; fp32, bf16 or fp16
+ *  causal      1: key j is visible to query i only if j <= kv_lens[b]-q_len+i
+ *  softcap     > 0: scores become softcap * tanh(scores / softcap) before the mask
+ *  out         [B, Hq, q_len, D] with strides out_stride_b/_h/_s (multiples of
+ *              4 elements; 8-byte aligned base)
+ *  workspace   helm_paged_prefill_workspace_bytes(...) bytes, 256-byte aligned,
+ *              any contents (may be NULL when that size is 0)
+ *  max_kv_len  the largest kv_lens entry: it sizes the split of the key range
+ *              (results do not depend on it)
+ * A row that sees no key gets zeros.  dtype: HELM_DTYPE_BF16 or FP16;
+ * head_dim 64 or 128.  Launches the prefill kernel and, when the key range is
+ * split, its merge kernel as a programmatic dependent.
+ */
+int64_t helm_paged_prefill_workspace_bytes(int batch, int q_len, int num_q_heads,
+                                           int num_kv_heads, int head_dim, int dtype,
+                                           int max_kv_len);
+int helm_paged_prefill_attention(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                 int64_t q_stride_s, const void* kv_pool, int64_t pool_pages,
+                                 const int32_t* page_table, int64_t pt_stride_b, int max_pages,
+                                 const int32_t* kv_lens, const void* mask, int mask_dtype,
+                                 int64_t mask_stride_b, int64_t mask_stride_q, void* out,
+                                 int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
+                                 void* workspace, int64_t workspace_bytes, int batch, int q_len,
+                                 int num_q_heads, int num_kv_heads, int head_dim, int page_size,
+                                 int dtype, int causal, float scale, float softcap, int max_kv_len,
+                                 void* stream);
+
+/*
  * Merges R partial attention states over disjoint key ranges:
  *     M = max_r lse[r];  w_r = exp(lse[r] - M)
  *     out = sum_r w_r * o[r] / sum_r w_r,   lse_out = M + log(sum_r w_r)

@@ -1,0 +1,161 @@
+"""Parity of the CUDA chunk-prefill attention (helm_paged_prefill_attention,
+through the C ABI) with the CPU oracle.
+
+A prefill chunk is, row by row, the reference's streaming attention
+(helm/runtime/kv_cache.py:469-555) for one query with the mask row of that
+query: the oracle (pinned to the reference by the golden fixtures in
+test_oracle.py) is called once per query position with mask[:, 0, s, :] plus
+the causal limit.  The pool is filled with NaN before the pages are written,
+so a stale row that leaked into a result would show up.
+
+Tolerances (fp32 accumulation; output in the model dtype, P rounded to it for
+the tensor-core P.V product):
+  bf16: |gpu - oracle| <= 1e-2 + 1e-2 |oracle|
+  fp16: |gpu - oracle| <= 2e-3 + 4e-3 |oracle|
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helm_b200 import _capi
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.bfloat16: (1e-2, 1e-2), torch.float16: (2e-3, 4e-3)}
+ORACLE_DT = {torch.bfloat16: 2, torch.float16: 1}
+
+
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    return torch.device("cuda:0")
+
+
+def _setup(dev, dtype, B, Hq, Hkv, D, P, lens, S, seed):
+    g = torch.Generator().manual_seed(seed)
+    maxp = max((l + P - 1) // P for l in lens)
+    slots = B * maxp + 5
+    pool = torch.full((slots, 2, Hkv, P, D), float("nan"), dtype=dtype)
+    perm = torch.randperm(slots, generator=g)[:B * maxp].view(B, maxp).to(torch.int32)
+    for b, L in enumerate(lens):
+        kv = torch.randn(2, Hkv, L, D, generator=g).to(dtype)
+        for j in range(0, L, P):
+            n = min(P, L - j)
+            pool[perm[b, j // P], :, :, :n] = kv[:, :, j:j + n]
+    q = torch.randn(B, Hq, S, D, generator=g).to(dtype)
+    return pool, perm, q, g
+
+
+def _oracle(pool, perm, q, lens, P, Hkv, mask, causal, softcap, scale):
+    """[B, Hq, S, D] fp32: the decode oracle once per query position."""
+    B, Hq, S, D = q.shape
+    T = max(lens)
+    bits = pool.view(torch.int16).numpy().view(np.uint16)
+    num_pages, page_used = oracle.dense_page_lists(lens, P, perm.shape[1])
+    out = np.zeros((B, Hq, S, D), np.float32)
+    for s in range(S):
+        m = np.zeros((B, T), np.float32)
+        if mask is not None:
+            mm = mask[:, 0, s, :T].float().numpy()
+            m += np.broadcast_to(mm, (B, T))
+        if causal:
+            for b, L in enumerate(lens):
+                m[b, L - S + s + 1:] = -np.inf
+        o, _ = oracle.paged_attention(q[:, :, s].float().numpy(), bits, ORACLE_DT[q.dtype],
+                                      perm.numpy(), num_pages, page_used, num_kv_heads=Hkv,
+                                      page_size=P, scale=scale, softcap=softcap, mask=m,
+                                      threads=8)
+        out[:, :, s] = o
+    return out
+
+
+def _chunk_mask(lens, S, dtype, pad=None):
+    """HELM's chunk-prefill mask (pipeline_runtime.py:96-112): queries at
+    [past, past+S) see keys <= their position, plus key padding."""
+    B, T = len(lens), max(lens)
+    mn = torch.finfo(dtype).min
+    m = torch.full((B, 1, S, T), mn, dtype=dtype)
+    for b, L in enumerate(lens):
+        past = L - S
+        for i in range(S):
+            m[b, 0, i, :past + i + 1] = 0
+        if pad and b in pad:
+            m[b, 0, :, :pad[b]] = m[b, 0, :, :pad[b]] + mn
+    return m
+
+
+CASES = [
+    # dtype, B, Hq, Hkv, D, P, lens, S, mask, causal, softcap
+    (torch.bfloat16, 2, 8, 2, 128, 16, [300, 517], 40, "helm", False, 0.0),
+    (torch.float16, 1, 4, 4, 64, 64, [130], 130, None, True, 0.0),
+    (torch.bfloat16, 3, 16, 8, 128, 32, [64, 1000, 65], 33, "fp32", True, 30.0),
+    (torch.bfloat16, 2, 8, 1, 64, 16, [50, 64], 50, None, True, 0.0),
+    (torch.bfloat16, 1, 8, 8, 128, 64, [4096], 16, None, True, 0.0),
+    (torch.float16, 2, 12, 4, 128, 16, [777, 129], 100, "helm", False, 0.0),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"case{i}" for i in range(len(CASES))])
+def test_prefill_kernel_matches_oracle(case):
+    dev = _cuda()
+    dtype, B, Hq, Hkv, D, P, lens, S, mask_kind, causal, softcap = case
+    pool, perm, q, g = _setup(dev, dtype, B, Hq, Hkv, D, P, lens, S, seed=len(lens) * 7 + S)
+    T = max(lens)
+    mask = None
+    if mask_kind == "helm":
+        mask = _chunk_mask(lens, S, dtype, pad={0: 7})
+    elif mask_kind == "fp32":
+        mask = (torch.rand(1, 1, S, T, generator=g) * 2 - 1).float()
+    scale = D ** -0.5
+    out = _capi.paged_prefill_attention(
+        q.to(dev), pool.to(dev), perm.to(dev), torch.tensor(lens, dtype=torch.int32, device=dev),
+        num_kv_heads=Hkv, page_size=P, scale=scale, max_kv_len=T,
+        mask=None if mask is None else mask.to(dev), causal=causal, softcap=softcap)
+    torch.cuda.synchronize()
+    assert _capi.device_status(dev) == 0
+    ref = _oracle(pool, perm, q, lens, P, Hkv, mask, causal, softcap, scale)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    atol, rtol = TOL[dtype]
+    err = np.abs(got - ref)
+    assert (err <= atol + rtol * np.abs(ref)).all(), err.max()
+
+
+def test_prefill_rows_without_keys_are_zero():
+    """A query row whose every key is masked with -inf gets zeros (the
+    reference's running max stays -inf there); the other rows are unaffected."""
+    dev = _cuda()
+    dtype, Hq, Hkv, D, P, lens, S = torch.bfloat16, 4, 2, 128, 16, [200], 8
+    pool, perm, q, _ = _setup(dev, dtype, 1, Hq, Hkv, D, P, lens, S, seed=3)
+    mask = torch.zeros(1, 1, S, lens[0], dtype=torch.float32)
+    mask[0, 0, 3] = -float("inf")
+    out = _capi.paged_prefill_attention(
+        q.to(dev), pool.to(dev), perm.to(dev), torch.tensor(lens, dtype=torch.int32, device=dev),
+        num_kv_heads=Hkv, page_size=P, scale=D ** -0.5, max_kv_len=lens[0], mask=mask.to(dev))
+    got = out.float().cpu()
+    assert torch.all(got[0, :, 3] == 0)
+    mask[0, 0, 3] = 0
+    ref = _oracle(pool, perm, q, lens, P, Hkv, mask, False, 0.0, D ** -0.5)
+    keep = [s for s in range(S) if s != 3]
+    err = (got[0, :, keep] - torch.from_numpy(ref)[0, :, keep]).abs()
+    assert err.max() <= 1e-2 + 1e-2 * float(np.abs(ref).max())
+
+
+def test_prefill_output_layout_and_arguments():
+    """The default output is a [B, Hq, S, D] view of a [B, S, Hq, D] buffer
+    (what the attention forward reshapes next); a strided caller buffer is
+    honoured; bad shapes are refused with a status, not a fault."""
+    dev = _cuda()
+    dtype, Hq, Hkv, D, P, lens, S = torch.bfloat16, 4, 2, 64, 16, [96], 32
+    pool, perm, q, _ = _setup(dev, dtype, 1, Hq, Hkv, D, P, lens, S, seed=5)
+    args = (q.to(dev), pool.to(dev), perm.to(dev), torch.tensor(lens, dtype=torch.int32,
+                                                                   device=dev))
+    kw = dict(num_kv_heads=Hkv, page_size=P, scale=D ** -0.5, max_kv_len=lens[0], causal=True)
+    a = _capi.paged_prefill_attention(*args, **kw)
+    assert a.shape == (1, Hq, S, D) and a.transpose(1, 2).is_contiguous()
+    b = torch.empty(1, Hq, S, D, dtype=dtype, device=dev)
+    _capi.paged_prefill_attention(*args, out=b, **kw)
+    assert torch.equal(a, b)
+    with pytest.raises(_capi.HelmError):
+        _capi.paged_prefill_attention(*args, **{**kw, "page_size": 8})

@@ -232,12 +232,16 @@ def test_cpu_pages_made_by_hand_with_cuda_query(dev):
            torch.bfloat16)
 
 
-def test_dense_prefill_path_matches_page_walk(dev):
-    """A 64-token prefill chunk over 320 cached tokens: the gather + attention
-    fast path equals the fp32 page walk within the bf16 tolerance, with HELM's
-    chunk-causal mask; with host-resident pages it declines (page walk used)."""
+@pytest.mark.parametrize("native", [False, True])
+def test_dense_prefill_path_matches_page_walk(dev, monkeypatch, native):
+    """A 64-token prefill chunk over 320 cached tokens: the device path
+    (gather + library attention by default, the native paged kernel with
+    HELM_B200_NATIVE_PREFILL=1 or a softcap) equals the fp32 page walk within
+    the bf16 tolerance, with HELM's chunk-causal mask; with host-resident
+    pages it declines (page walk used)."""
     from helm_b200.runtime.kv_cache import _prefill_over_pages
     from helm_b200.runtime.kv_offload import _prefill_dense_pages
+    monkeypatch.setenv("HELM_B200_NATIVE_PREFILL", "1" if native else "0")
     torch.manual_seed(11)
     H, D, P, T, S = 2, 64, 16, 320, 64
     for watermark, expect_fast in ((10 ** 12, True), (2 * 2 * H * P * D * 2, False)):
@@ -252,13 +256,14 @@ def test_dense_prefill_path_matches_page_walk(dev):
         j = torch.arange(T, device=dev).view(1, T)
         mask = torch.where(j <= past + i, 0.0, torch.finfo(torch.bfloat16).min)
         mask = mask.to(torch.bfloat16).view(1, 1, S, T)
-        fast = _prefill_dense_pages([mgr], q, 0, D ** -0.5, mask)
-        ref = _prefill_over_pages(q, [mgr.iterate_layer_pages(0)], D ** -0.5, mask, None)
-        if expect_fast:
-            assert fast is not None
-            _close(fast, ref, torch.bfloat16)
-        else:
-            assert fast is None
+        for softcap in ((None, 30.0) if native else (None,)):
+            fast = _prefill_dense_pages([mgr], q, 0, D ** -0.5, mask, softcap)
+            ref = _prefill_over_pages(q, [mgr.iterate_layer_pages(0)], D ** -0.5, mask, softcap)
+            if expect_fast:
+                assert fast is not None
+                _close(fast, ref, torch.bfloat16)
+            else:
+                assert fast is None
 
 
 def test_gemma2_sliding_window_known_answers(dev):
