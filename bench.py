@@ -623,7 +623,11 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
     in place) and, beside it, the path it replaces: gather_kv to dense K/V +
     torch SDPA with the mask.  value = attention TFLOP/s of the native kernel
     (4 * S * Hq * T * D per call, every key of every row computed, as the
-    reference's masked branch does)."""
+    reference's masked branch does).  Timed: the tcgen05 kernel (the default;
+    HELM_B200_PREFILL_KERNEL=mma selects the mma.sync one) as
+    _prefill_dense_pages calls it for HELM's chunk mask, which it recognises
+    as chunk-causal (value); beside it the same kernel reading the mask, the
+    mma.sync kernel and the gather + SDPA path."""
     import torch.nn.functional as F
 
     from helm_b200 import _capi
@@ -664,12 +668,27 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
         torch.cuda.synchronize(dev)
         return e0.elapsed_time(e1) / n
 
+    def native_causal():  # HELM's chunk mask as _prefill_dense_pages passes it
+        return _capi.paged_prefill_attention(q, pool, table, lens, num_kv_heads=Hkv, page_size=Pg,
+                                             scale=scale, max_kv_len=Tk, causal=True)
+
     steps = args.steps if args.steps_given else 10
-    a = native().float()
+    a = native_causal().float()
     b = gathered().float()
     diff = float((a - b).abs().max())
-    ms = timed(native, steps)
+    diff_mask = float((native().float() - b).abs().max())
+    ms = timed(native_causal, steps)
+    ms_mask = timed(native, max(1, steps // 2))
     ms_ref = timed(gathered, max(1, steps // 2))
+    prev = os.environ.get("HELM_B200_PREFILL_KERNEL")
+    os.environ["HELM_B200_PREFILL_KERNEL"] = "mma"  # the mma.sync kernel, for comparison
+    try:
+        ms_mma = timed(native_causal, max(1, steps // 2))
+    finally:
+        if prev is None:
+            del os.environ["HELM_B200_PREFILL_KERNEL"]
+        else:
+            os.environ["HELM_B200_PREFILL_KERNEL"] = prev
     if rank != 0:
         return
     flop = 4.0 * S * Hq * Tk * D
@@ -686,8 +705,14 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
                       "data": "synthetic",
                       "config": {"workload": f"prefill: 1 x {S} queries x {Hq}/{Hkv} heads over "
                                              f"{Tk} cached tokens, page {Pg}, HELM chunk mask",
+                                 "kernel": "tcgen05" if os.environ.get(
+                                     "HELM_B200_PREFILL_KERNEL") != "mma" else "mma.sync",
+                                 "mask": "recognised as chunk-causal (causal limit, no mask reads)",
+                                 "ms_with_mask_read": ms_mask,
                                  "gather_sdpa_ms": ms_ref, "speedup_vs_gather_sdpa": ms_ref / ms,
-                                 "max_abs_diff_vs_gather_sdpa": diff},
+                                 "mma_sync_kernel_ms": ms_mma,
+                                 "max_abs_diff_vs_gather_sdpa": diff,
+                                 "max_abs_diff_mask_read_vs_gather_sdpa": diff_mask},
                       "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak,
                                    "unit": "TFLOP/s", "frac": tflops / peak, "traffic": None,
                                    "peak_source": src},

@@ -3,6 +3,7 @@
 #include "common.cuh"
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "kv_append.cu"
@@ -10,6 +11,7 @@
 #include "paged_attention.cu"
 #include "paged_attention_noalloc.cu"
 #include "paged_prefill.cu"
+#include "paged_prefill_tc.cu"
 #include "peer_exchange.cu"
 #include "decode_gemv.cu"
 

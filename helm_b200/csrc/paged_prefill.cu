@@ -33,7 +33,9 @@
 //
 // This file is part of the single translation unit helm_b200.cu and uses the
 // helpers of paged_attention.cu (get_encode_fn, mask_log2, kLog2e), which is
-// included before it.
+// included before it.  paged_prefill_tc.cu, included after it, holds the
+// tensor-memory (tcgen05) form of the same computation and the C entry points
+// that choose between the two.
 
 namespace helm {
 
@@ -84,8 +86,8 @@ struct PfLayout {
 
 // Keys of unit (b, rb) that any of its rows may see: the sequence's length,
 // clamped to its page-table row, and with the causal limit of the block's
-// last row.
-__device__ __forceinline__ int unit_keys(const PrefillArgs& a, int b, int rb) {
+// last row (row blocks of `rpu` rows).
+__device__ __forceinline__ int unit_keys(const PrefillArgs& a, int b, int rb, int rpu) {
   int kv = a.kv_lens[b];
   const int64_t cap = static_cast<int64_t>(a.max_pages) * a.page_size;
   if (kv < 0) kv = 0;
@@ -94,7 +96,7 @@ __device__ __forceinline__ int unit_keys(const PrefillArgs& a, int b, int rb) {
     kv = static_cast<int>(cap);
   }
   if (a.causal) {
-    const int r_last = min(a.rows, (rb + 1) * kPfRows) - 1;
+    const int r_last = min(a.rows, (rb + 1) * rpu) - 1;
     const int lim = kv - a.q_len + r_last / a.group + 1;
     kv = max(0, min(kv, lim));
   }
@@ -129,7 +131,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const int split = rest % a.splits;
   const int pair = rest / a.splits;
   const int b = pair / a.hkv, h = pair - (pair / a.hkv) * a.hkv;
-  const int kv_u = unit_keys(a, b, rb);
+  const int kv_u = unit_keys(a, b, rb, kPfRows);
   const int n_tiles = (kv_u + kPfTile - 1) / kPfTile;
   const int t_begin = static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
   const int t_end = static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
@@ -399,12 +401,12 @@ __global__ void __launch_bounds__(kPfThreads, 2)
 }
 
 // Merges the splits of every unit: CTA (unit, chunk) owns 256 (row, 4-column)
-// elements of the unit's 64 x D block and combines the `splits` partial
+// elements of the unit's RPU x D block and combines the `splits` partial
 // states of each (running rescaled sum, the loads of kPfMergeBatch splits in
-// flight per thread).
+// flight per thread).  Partials are [unit * splits + split][RPU rows][D].
 constexpr int kPfMergeBatch = 4;
 
-template <typename T, int D>
+template <typename T, int D, int RPU>
 __global__ void __launch_bounds__(kPfMergeThreads) merge_prefill_splits_kernel(const PrefillArgs a) {
   constexpr int D4 = D / 4;
   // every thread waits for the prefill kernel (complete and visible)
@@ -413,8 +415,8 @@ __global__ void __launch_bounds__(kPfMergeThreads) merge_prefill_splits_kernel(c
   const int rb = unit % a.row_blocks, pair = unit / a.row_blocks;
   const int e = blockIdx.y * kPfMergeThreads + threadIdx.x;
   const int row = e / D4, d4 = e - (e / D4) * D4;
-  if (row >= kPfRows) return;
-  const int r = rb * kPfRows + row;
+  if (row >= RPU) return;
+  const int r = rb * RPU + row;
   if (r >= a.rows) return;
   const int b = pair / a.hkv, h = pair - (pair / a.hkv) * a.hkv;
   const int s = r / a.group, qh = h * a.group + (r - s * a.group);
@@ -429,7 +431,7 @@ __global__ void __launch_bounds__(kPfMergeThreads) merge_prefill_splits_kernel(c
       ml[i] = make_float2(-INFINITY, 0.f);
       ov[i] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (k0 + i < a.splits) {
-        const int64_t rec = (part0 + k0 + i) * kPfRows + row;
+        const int64_t rec = (part0 + k0 + i) * RPU + row;
         ml[i] = __ldcg(reinterpret_cast<const float2*>(a.part_ml + rec * 2));
         ov[i] = __ldcg(reinterpret_cast<const float4*>(a.part_o + rec * D + d4 * 4));
       }
@@ -491,17 +493,17 @@ struct PrefillPlan {
 // minimises whole waves x tiles per split, plus two tiles' worth per extra
 // pass (the partial write and the merge).
 PrefillPlan plan_prefill(int batch, int q_len, int hq, int hkv, int d, int max_kv_len,
-                         int ctas_per_sm) {
+                         int ctas_per_sm, int rpu) {
   PrefillPlan p;
   const int group = hq / hkv;
   const int64_t rows = static_cast<int64_t>(q_len) * group;
-  p.row_blocks = static_cast<int>((rows + kPfRows - 1) / kPfRows);
+  p.row_blocks = static_cast<int>((rows + rpu - 1) / rpu);
   p.units = static_cast<int64_t>(batch) * hkv * p.row_blocks;
   const int64_t slots = static_cast<int64_t>(num_sms_current_device()) * std::max(1, ctas_per_sm);
   const int64_t tiles = std::max<int64_t>(1, (static_cast<int64_t>(max_kv_len) + kPfTile - 1) / kPfTile);
   int64_t best_cost = -1;
   for (int sp = 1; sp <= kPfMaxSplits && sp <= tiles; ++sp) {
-    if (sp > 1 && p.units * sp * kPfRows * d * 4 > kPfMaxPartialBytes) break;
+    if (sp > 1 && p.units * sp * rpu * d * 4 > kPfMaxPartialBytes) break;
     const int64_t waves = (p.units * sp + slots - 1) / slots;
     const int64_t cost = waves * ((tiles + sp - 1) / sp) + (sp > 1 ? 2 : 0);
     if (best_cost < 0 || cost < best_cost) {
@@ -510,16 +512,35 @@ PrefillPlan plan_prefill(int batch, int q_len, int hq, int hkv, int d, int max_k
     }
   }
   auto up = [](int64_t x) { return ((x + 255) / 256) * 256; };
-  p.o_bytes = up(p.units * p.splits * kPfRows * d * 4);
-  p.ml_bytes = up(p.units * p.splits * kPfRows * 2 * 4);
+  p.o_bytes = up(p.units * p.splits * rpu * d * 4);
+  p.ml_bytes = up(p.units * p.splits * rpu * 2 * 4);
   return p;
+}
+
+// TMA map over the pool viewed as [slots * 2 * Hkv * page_size rows, D]:
+// boxes of 16 rows x 64 columns, 128-byte swizzle.
+template <typename T, int D>
+bool encode_pool_map(const void* pool, int64_t pool_rows, CUtensorMap* map) {
+  EncodeTiledFn encode = get_encode_fn();
+  if (encode == nullptr) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(pool_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
+  cuuint32_t box[2] = {64, 16};
+  cuuint32_t estride[2] = {1, 1};
+  const CUtensorMapDataType dt = std::is_same<T, __nv_bfloat16>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode(map, dt, 2, const_cast<void*>(pool), dims, strides, box, estride,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
 }
 
 template <typename T, int D>
 int launch_prefill(PrefillArgs a, const void* pool, int64_t pool_rows, int max_kv_len,
                    void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
   const int ctas = prefill_ctas_per_sm<T, D>();
-  const PrefillPlan plan = plan_prefill(a.batch, a.q_len, a.hq, a.hkv, D, max_kv_len, ctas);
+  const PrefillPlan plan = plan_prefill(a.batch, a.q_len, a.hq, a.hkv, D, max_kv_len, ctas, kPfRows);
   if (workspace_bytes < plan.total()) return HELM_ERR_WORKSPACE;
   if (plan.total() > 0 && workspace == nullptr) return HELM_ERR_WORKSPACE;
   a.row_blocks = plan.row_blocks;
@@ -531,20 +552,8 @@ int launch_prefill(PrefillArgs a, const void* pool, int64_t pool_rows, int max_k
   if (grid <= 0) return HELM_OK;
   if (grid >= (int64_t(1) << 31)) return HELM_ERR_UNSUPPORTED;
 
-  EncodeTiledFn encode = get_encode_fn();
-  if (encode == nullptr) return HELM_ERR_CUDA;
   CUtensorMap map;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(pool_rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(D) * 2};
-  cuuint32_t box[2] = {64, 16};
-  cuuint32_t estride[2] = {1, 1};
-  const CUtensorMapDataType dt = std::is_same<T, __nv_bfloat16>::value
-                                     ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  if (encode(&map, dt, 2, const_cast<void*>(pool), dims, strides, box, estride,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return HELM_ERR_CUDA;
+  if (!encode_pool_map<T, D>(pool, pool_rows, &map)) return HELM_ERR_CUDA;
   paged_prefill_kernel<T, D><<<static_cast<unsigned>(grid), kPfThreads,
                                PfLayout<D>::smem_bytes(), stream>>>(map, a);
   if (cudaGetLastError() != cudaSuccess) return HELM_ERR_CUDA;
@@ -560,7 +569,7 @@ int launch_prefill(PrefillArgs a, const void* pool, int64_t pool_rows, int max_k
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, merge_prefill_splits_kernel<T, D>, a) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, merge_prefill_splits_kernel<T, D, kPfRows>, a) != cudaSuccess)
     return HELM_ERR_CUDA;
   return HELM_OK;
 }
@@ -582,98 +591,3 @@ int prefill_dispatch(int head_dim, const PrefillArgs& a, const void* pool, int64
 
 }  // namespace helm
 
-extern "C" int64_t helm_paged_prefill_workspace_bytes(int batch, int q_len, int num_q_heads,
-                                                      int num_kv_heads, int head_dim, int dtype,
-                                                      int max_kv_len) {
-  using namespace helm;
-  if (batch <= 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
-      num_q_heads % num_kv_heads != 0 || max_kv_len < 0)
-    return 0;
-  int ctas = 1;
-  const bool bf = dtype == HELM_DTYPE_BF16;
-  if (head_dim == 64)
-    ctas = bf ? prefill_ctas_per_sm<__nv_bfloat16, 64>() : prefill_ctas_per_sm<__half, 64>();
-  else if (head_dim == 128)
-    ctas = bf ? prefill_ctas_per_sm<__nv_bfloat16, 128>() : prefill_ctas_per_sm<__half, 128>();
-  else
-    return 0;
-  return plan_prefill(batch, q_len, num_q_heads, num_kv_heads, head_dim, max_kv_len, ctas).total();
-}
-
-extern "C" int helm_paged_prefill_attention(
-    const void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s, const void* kv_pool,
-    int64_t pool_pages, const int32_t* page_table, int64_t pt_stride_b, int max_pages,
-    const int32_t* kv_lens, const void* mask, int mask_dtype, int64_t mask_stride_b,
-    int64_t mask_stride_q, void* out, int64_t out_stride_b, int64_t out_stride_h,
-    int64_t out_stride_s, void* workspace, int64_t workspace_bytes, int batch, int q_len,
-    int num_q_heads, int num_kv_heads, int head_dim, int page_size, int dtype, int causal,
-    float scale, float softcap, int max_kv_len, void* stream) {
-  using namespace helm;
-  if (q == nullptr || kv_pool == nullptr || page_table == nullptr || kv_lens == nullptr ||
-      out == nullptr)
-    return HELM_ERR_INVALID_ARGUMENT;
-  if (batch <= 0 || q_len <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || page_size <= 0 ||
-      max_pages < 0 || pool_pages <= 0 || max_kv_len < 0)
-    return HELM_ERR_INVALID_ARGUMENT;
-  if (num_q_heads % num_kv_heads != 0) return HELM_ERR_INVALID_ARGUMENT;
-  if (dtype != HELM_DTYPE_BF16 && dtype != HELM_DTYPE_FP16) return HELM_ERR_UNSUPPORTED;
-  if (head_dim != 64 && head_dim != 128) return HELM_ERR_UNSUPPORTED;
-  if (page_size % 16 != 0) return HELM_ERR_UNSUPPORTED;  // 16-key boxes stay inside a page
-  if (mask != nullptr && mask_dtype != HELM_DTYPE_FP32 && mask_dtype != HELM_DTYPE_BF16 &&
-      mask_dtype != HELM_DTYPE_FP16)
-    return HELM_ERR_INVALID_ARGUMENT;
-  // q and out are accessed as 32-bit words, the pool through TMA (16-byte rule)
-  if ((reinterpret_cast<uintptr_t>(q) & 3) || (q_stride_b & 1) || (q_stride_h & 1) ||
-      (q_stride_s & 1))
-    return HELM_ERR_ALIGNMENT;
-  if ((reinterpret_cast<uintptr_t>(out) & 7) || (out_stride_b & 3) || (out_stride_h & 3) ||
-      (out_stride_s & 3))
-    return HELM_ERR_ALIGNMENT;
-  if ((reinterpret_cast<uintptr_t>(kv_pool) & 15) || (reinterpret_cast<uintptr_t>(workspace) & 255))
-    return HELM_ERR_ALIGNMENT;
-  const int64_t pool_rows = pool_pages * 2 * num_kv_heads * static_cast<int64_t>(page_size);
-  if (pool_rows >= (int64_t(1) << 31)) return HELM_ERR_UNSUPPORTED;
-  if (static_cast<int64_t>(max_pages) * page_size >= (int64_t(1) << 30)) return HELM_ERR_UNSUPPORTED;
-
-  PrefillArgs a;
-  a.q = q;
-  a.q_sb = q_stride_b;
-  a.q_sh = q_stride_h;
-  a.q_ss = q_stride_s;
-  a.pool_pages = pool_pages;
-  a.page_table = page_table;
-  a.pt_sb = pt_stride_b;
-  a.max_pages = max_pages;
-  a.kv_lens = kv_lens;
-  a.mask = mask;
-  a.mask_dtype = mask_dtype;
-  a.mask_sb = mask_stride_b;
-  a.mask_sq = mask_stride_q;
-  a.out = out;
-  a.o_sb = out_stride_b;
-  a.o_sh = out_stride_h;
-  a.o_ss = out_stride_s;
-  a.part_o = nullptr;
-  a.part_ml = nullptr;
-  a.batch = batch;
-  a.q_len = q_len;
-  a.hq = num_q_heads;
-  a.hkv = num_kv_heads;
-  a.group = num_q_heads / num_kv_heads;
-  a.page_size = page_size;
-  a.rows = q_len * a.group;
-  a.row_blocks = 0;
-  a.splits = 1;
-  a.causal = causal != 0 ? 1 : 0;
-  a.scale = scale;
-  a.scale_log2 = scale * kLog2e;
-  a.softcap = softcap;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  int rc = dtype == HELM_DTYPE_BF16
-               ? prefill_dispatch<__nv_bfloat16>(head_dim, a, kv_pool, pool_rows, max_kv_len,
-                                                 workspace, workspace_bytes, s)
-               : prefill_dispatch<__half>(head_dim, a, kv_pool, pool_rows, max_kv_len, workspace,
-                                          workspace_bytes, s);
-  if (rc == HELM_ERR_CUDA) set_last_cuda_error(cudaGetLastError());
-  return rc;
-}

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import math
 import os
+import weakref
 from dataclasses import dataclass
 from types import MethodType
 from typing import Optional
@@ -201,6 +202,39 @@ def _append_prefill_batched(kvcms, k, v, layer_idx: int) -> list:
     return past_lengths
 
 
+_CAUSAL_MEMO: list = []  # [(weakref to the caller's mask tensor, key, verdict)], newest last
+
+
+def _is_chunk_causal(attention_mask: torch.Tensor, mask: torch.Tensor, lens: np.ndarray,
+                     S: int) -> bool:
+    """True when mask [B|1, 1, S, T] (a slice of attention_mask) is HELM's
+    chunk-causal mask without padding (pipeline_runtime.py:96-112): 0 where key
+    j <= lens[b] - S + i, and <= -1e4 everywhere else.  Every row then keeps
+    its own key, so the masked keys get weight exp(<= -1e4) = 0 in fp32 and
+    the kernel's causal limit gives the same result without reading the mask.
+    Decided once per mask tensor and lengths (one device reduction + sync):
+    the same mask object serves every layer of a chunk."""
+    base = attention_mask._base if attention_mask._base is not None else attention_mask
+    key = (tuple(mask.shape), tuple(mask.stride()), mask.storage_offset(), base._version,
+           lens.tobytes(), S)
+    for ref, k, verdict in _CAUSAL_MEMO:
+        if ref() is base and k == key:
+            return verdict
+    B, T = mask.shape[0], mask.shape[3]
+    verdict = False
+    if B == len(lens) or bool(np.all(lens == lens[0])):
+        dev = mask.device
+        past = torch.as_tensor(lens[:B].astype(np.int64) - S, device=dev).view(-1, 1, 1)
+        i = torch.arange(S, device=dev).view(1, S, 1)
+        j = torch.arange(T, device=dev).view(1, 1, T)
+        allowed = j <= past + i
+        m = mask[:, 0]
+        verdict = bool(torch.where(allowed, m == 0, m <= -1e4).all())
+    _CAUSAL_MEMO.append((weakref.ref(base), key, verdict))
+    del _CAUSAL_MEMO[:-4]
+    return verdict
+
+
 def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
                          attention_mask: Optional[torch.Tensor],
                          softcap: Optional[float] = None) -> Optional[torch.Tensor]:
@@ -240,8 +274,10 @@ def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
                                     and mask.dtype in (torch.float32, torch.bfloat16,
                                                        torch.float16))))
     if native and (softcap is not None or os.environ.get("HELM_B200_NATIVE_PREFILL") == "1"):
+        causal = mask is not None and _is_chunk_causal(attention_mask, mask, lens, q.shape[2])
         return _capi.paged_prefill_attention(q, pool.storage, slots, kl, num_kv_heads=Hkv,
-                                             page_size=P, scale=scale, max_kv_len=T, mask=mask,
+                                             page_size=P, scale=scale, max_kv_len=T,
+                                             mask=None if causal else mask, causal=causal,
                                              softcap=softcap)
     if softcap is not None:
         return None

@@ -1,5 +1,6 @@
 """Parity of the CUDA chunk-prefill attention (helm_paged_prefill_attention,
-through the C ABI) with the CPU oracle.
+through the C ABI) with the CPU oracle, for both of its kernels: the tcgen05
+one (default) and the mma.sync one (HELM_B200_PREFILL_KERNEL=mma).
 
 A prefill chunk is, row by row, the reference's streaming attention
 (helm/runtime/kv_cache.py:469-555) for one query with the mask row of that
@@ -96,8 +97,14 @@ CASES = [
 ]
 
 
+@pytest.fixture(params=["tc", "mma"])
+def kernel(request, monkeypatch):
+    monkeypatch.setenv("HELM_B200_PREFILL_KERNEL", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("case", CASES, ids=[f"case{i}" for i in range(len(CASES))])
-def test_prefill_kernel_matches_oracle(case):
+def test_prefill_kernel_matches_oracle(case, kernel):
     dev = _cuda()
     dtype, B, Hq, Hkv, D, P, lens, S, mask_kind, causal, softcap = case
     pool, perm, q, g = _setup(dev, dtype, B, Hq, Hkv, D, P, lens, S, seed=len(lens) * 7 + S)
@@ -122,7 +129,7 @@ def test_prefill_kernel_matches_oracle(case):
     assert (err <= atol + rtol * np.abs(ref)).all(), err.max()
 
 
-def test_prefill_rows_without_keys_are_zero():
+def test_prefill_rows_without_keys_are_zero(kernel):
     """A query row whose every key is masked with -inf gets zeros (the
     reference's running max stays -inf there); the other rows are unaffected."""
     dev = _cuda()
@@ -142,7 +149,7 @@ def test_prefill_rows_without_keys_are_zero():
     assert err.max() <= 1e-2 + 1e-2 * float(np.abs(ref).max())
 
 
-def test_prefill_output_layout_and_arguments():
+def test_prefill_output_layout_and_arguments(kernel):
     """The default output is a [B, Hq, S, D] view of a [B, S, Hq, D] buffer
     (what the attention forward reshapes next); a strided caller buffer is
     honoured; bad shapes are refused with a status, not a fault."""

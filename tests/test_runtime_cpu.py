@@ -327,3 +327,27 @@ def test_host_tier_placement_matches_reference(placement_golden):
             continue
         snaps = replay(sc)
         assert snaps == entry["snapshots"], sc["name"]
+
+
+def test_chunk_causal_mask_detection():
+    """HELM's chunk-prefill mask without padding (pipeline_runtime.py:96-112)
+    is recognised as the causal limit (the native kernel then reads no mask);
+    padding, a visible future key or other lengths are not."""
+    import numpy as np
+    from helm_b200.runtime.kv_offload import _is_chunk_causal
+    S, T = 6, 20
+    i = torch.arange(S).view(S, 1)
+    j = torch.arange(T).view(1, T)
+    for dtype in (torch.bfloat16, torch.float16, torch.float32):
+        mn = torch.finfo(dtype).min
+        m = torch.where(j <= T - S + i, 0.0, mn).to(dtype).view(1, 1, S, T)
+        assert _is_chunk_causal(m, m, np.array([T], np.int32), S)
+        two = m.expand(2, 1, S, T)
+        assert _is_chunk_causal(two, two, np.array([T, T], np.int32), S)
+        padded = m.clone()
+        padded[0, 0, :, :3] = mn
+        assert not _is_chunk_causal(padded, padded, np.array([T], np.int32), S)
+        future = m.clone()
+        future[0, 0, 0, T - 1] = 0
+        assert not _is_chunk_causal(future, future, np.array([T], np.int32), S)
+        assert not _is_chunk_causal(m, m, np.array([T - 1], np.int32), S)
