@@ -243,17 +243,19 @@ def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
 
     Two device paths, both with HELM's additive mask (chunk-causal + padding,
     kv_offload.py:206-227):
-      * K/V gathered to dense [B, Hkv, T, D] by one gather_kv launch, then one
-        library attention (torch SDPA) over them: the default, ~5x faster than
-        the native kernel at long context on B200 (the library attention runs
-        on the tcgen05 tensor cores; the native kernel on mma.sync);
       * helm_paged_prefill_attention, reading K/V in place from the pool (no
-        dense copy): used for soft-capped scores, which the library call does
-        not take, and for every chunk when HELM_B200_NATIVE_PREFILL=1.
-    The native kernel needs bf16/fp16, head dim 64 or 128 and a page size that
-    is a multiple of 16.  None when the page lists are ragged or partly on the
-    host, or when a softcap needs the native kernel and the shape is not one
-    of those (the caller walks the pages)."""
+        dense copy; tcgen05 kernel): used when the mask is HELM's chunk-causal
+        mask (recognised once per mask, then applied as the kernel's causal
+        limit without reading it), when there is no mask, and for soft-capped
+        scores;
+      * K/V gathered to dense [B, Hkv, T, D] by one gather_kv launch, then one
+        library attention (torch SDPA): used for other masks (key padding),
+        which the kernel would read element by element.
+    HELM_B200_NATIVE_PREFILL=1 sends every chunk to the kernel, =0 every chunk
+    without softcap to the library.  The kernel needs bf16/fp16, head dim 64
+    or 128 and a page size that is a multiple of 16.  None when the page lists
+    are ragged or partly on the host, or when a softcap needs the kernel and
+    the shape is not one of those (the caller walks the pages)."""
     dev = q.device
     pool = _device_pool(kvcms, dev)
     t = _layer_tables(kvcms, layer_idx, pool)
@@ -273,8 +275,12 @@ def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
                                     and mask.shape[2] == q.shape[2] and mask.shape[3] == T
                                     and mask.dtype in (torch.float32, torch.bfloat16,
                                                        torch.float16))))
-    if native and (softcap is not None or os.environ.get("HELM_B200_NATIVE_PREFILL") == "1"):
+    choice = os.environ.get("HELM_B200_NATIVE_PREFILL")
+    use_kernel = causal = False
+    if native and (choice != "0" or softcap is not None):
         causal = mask is not None and _is_chunk_causal(attention_mask, mask, lens, q.shape[2])
+        use_kernel = softcap is not None or choice == "1" or mask is None or causal
+    if use_kernel:
         return _capi.paged_prefill_attention(q, pool.storage, slots, kl, num_kv_heads=Hkv,
                                              page_size=P, scale=scale, max_kv_len=T,
                                              mask=None if causal else mask, causal=causal,
