@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   uint64_t* bar_sfree = bar_s + 1;       // the 4 row warps have read S
   uint64_t* bar_p = bar_s + 2;           // [2] P buffer written (4 row warps)
   uint64_t* bar_o = bar_s + 4;           // [2] P.V of tiles with that parity completed
+  uint64_t* bar_fin = bar_s + 6;         // drain after an abandoned wait: all MMAs done
 
   // blockIdx.x = ((b * hkv + h) * splits + split) * row_blocks + rb
   const int rb = blockIdx.x % a.row_blocks;
@@ -273,6 +274,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     mbar_init(&bar_p[1], kTcSoftWarps);
     mbar_init(&bar_o[0], 1);
     mbar_init(&bar_o[1], 1);
+    mbar_init(bar_fin, 1);
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -311,6 +313,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   bool ok = true;
   if (warp == kTcSoftWarps) {
     // ============================== loads + MMAs ==============================
+    int loads_issued = 0, loads_seen = 0;  // tiles whose TMA was issued / observed complete
+    bool mma_issued = false;
     const int64_t kv_rows = static_cast<int64_t>(a.hkv) * a.page_size;
     const uint32_t sq_addr = smem_addr(sq), skv_addr = smem_addr(skv);
     auto fetch = [&](int i, int& slot, bool& okg) {
@@ -379,6 +383,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       if (jj + kTcNS < n) {
         if (!warp_wait(&empty[st], (jj / kTcNS) & 1)) return false;
         issue(jj + kTcNS, slot, okg);
+        ++loads_issued;
       }
       return true;
     };
@@ -389,12 +394,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         bool okg;
         fetch(i, slot, okg);
         issue(i, slot, okg);
+        ++loads_issued;
       }
     }
     for (int j = 0; j < n; ++j) {
       const int st = j % kTcNS;
-      if (!warp_wait(&full[st], (j / kTcNS) & 1) ||
-          (j > 0 && !warp_wait(bar_sfree, (j - 1) & 1))) {
+      if (!warp_wait(&full[st], (j / kTcNS) & 1)) {
+        ok = false;
+        break;
+      }
+      loads_seen = j + 1;
+      if (j > 0 && !warp_wait(bar_sfree, (j - 1) & 1)) {
         ok = false;
         break;
       }
@@ -411,6 +421,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         }
         umma_commit(bar_s);
       }
+      mma_issued = true;
       __syncwarp();
       if (j > 0 && !do_pv(j - 1)) {
         ok = false;
@@ -422,6 +433,17 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       // the row warps wait for this last P.V before reading O; wait here as
       // well so that tensor memory is idle before it is released
       if (ok) ok = warp_wait(&bar_o[(n - 1) & 1], ((n - 1) >> 1) & 1);
+    }
+    if (!ok) {
+      // a wait was abandoned (reported): before the CTA releases its tensor
+      // memory and exits, wait (bounded) for the MMAs and TMA loads it issued
+      if (mma_issued) {
+        if (lane == 0) umma_commit(bar_fin);
+        __syncwarp();
+        warp_wait(bar_fin, 0);
+      }
+      for (int i = loads_seen; i < loads_issued; ++i)
+        warp_wait(&full[i % kTcNS], (i / kTcNS) & 1);
     }
   } else {
     // ================================ row warps ================================
