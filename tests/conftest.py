@@ -41,3 +41,18 @@ def placement_golden():
 @pytest.fixture(scope="session")
 def norm_rope_golden():
     return np.load(os.path.join(GOLDEN, "norm_rope.npz"))
+
+
+@pytest.fixture(scope="session")
+def prefill_golden():
+    z = np.load(os.path.join(GOLDEN, "prefill.npz"))
+    cases = {}
+    for name in z["names"]:
+        name = str(name)
+        pre = name + "/"
+        c = {k[len(pre):]: z[k] for k in z.files if k.startswith(pre)}
+        Hq, Hkv, D, P, S, is_fp16 = (int(x) for x in c["meta"])
+        c.update(Hq=Hq, Hkv=Hkv, D=D, P=P, S=S, dtype="float16" if is_fp16 else "bfloat16",
+                 softcap_f=float(c["softcap"][0]))
+        cases[name] = c
+    return cases

@@ -1,6 +1,7 @@
 """Generates the golden fixtures in tests/golden/ by running the HELM reference.
 
     PYTHONPATH=<helm checkout> python tests/golden/make_golden.py [--ref <helm checkout>]
+        [--only attention|placement|norm_rope|prefill]
 
 Everything here executes the reference's own code on seeded inputs and stores
 inputs plus the reference's outputs:
@@ -16,6 +17,11 @@ inputs plus the reference's outputs:
                   .device.type), so no GPU is needed
   norm_rope.npz   transformers' Qwen3RMSNorm + apply_rotary_pos_emb as called
                   by the reference's Qwen3 attention patch (kv_offload.py:368-373)
+  prefill.npz     perform_streaming_attention with q_len > 1: a prefill chunk
+                  (the last S positions of each sequence, already in the
+                  pages) under HELM's chunk-prefill mask
+                  (pipeline_runtime.py:96-112), as _stream_prefill_batched
+                  calls it (kv_offload.py:206-227)
 
 The fixtures are committed; this script is only needed to regenerate them.
 """
@@ -366,16 +372,113 @@ def make_norm_rope(ref, out_path: str):
     np.savez_compressed(out_path, **arrays)
 
 
+# ------------------------------------------------------------------- prefill --
+def _chunk_mask(lens, S, T, dtype, pad=None):
+    """HELM's chunk-prefill mask, built the way PipelineRuntime builds it
+    (pipeline_runtime.py:96-112): a query at position past + i sees keys
+    <= past + i; key padding adds finfo.min on padded keys."""
+    min_val = torch.finfo(dtype).min
+    B = len(lens)
+    masks = []
+    for b in range(B):
+        past = lens[b] - S
+        q_idx = torch.arange(S).view(S, 1)
+        k_idx = torch.arange(T).view(1, T)
+        m = torch.where(k_idx <= past + q_idx, torch.zeros((), dtype=dtype),
+                        torch.full((), min_val, dtype=dtype))
+        if pad and b in pad:
+            keys = torch.ones(T, dtype=dtype)
+            keys[:pad[b]] = 0
+            m = m + ((1.0 - keys) * min_val).view(1, T)
+        masks.append(m)
+    return torch.stack(masks).view(B, 1, S, T)
+
+
+def _prefill_cases():
+    c = []
+    c.append(("chunk_causal_bf16_d128_p16",
+              dict(Hq=8, Hkv=2, D=128, P=16, lens=[200], S=40)))
+    c.append(("chunk_padded_bf16_d64_p16",
+              dict(Hq=4, Hkv=4, D=64, P=16, lens=[150, 150], S=30, pad={0: 5})))
+    c.append(("chunk_softcap_fp16_d128_p64",
+              dict(Hq=4, Hkv=2, D=128, P=64, lens=[130], S=33, softcap=30.0,
+                   dtype="float16")))
+    c.append(("first_chunk_gqa8_d64_p32",
+              dict(Hq=8, Hkv=1, D=64, P=32, lens=[100], S=100)))
+    return c
+
+
+def make_prefill(ref, out_path: str):
+    from helm.runtime.kv_cache import KVPage, perform_streaming_attention
+    gen = torch.Generator().manual_seed(4321)
+    arrays = {}
+    names = []
+    for name, s in _prefill_cases():
+        dtype = getattr(torch, s.get("dtype", "bfloat16"))
+        Hq, Hkv, D, P, S = s["Hq"], s["Hkv"], s["D"], s["P"], s["S"]
+        lens = s["lens"]
+        B, T = len(lens), max(lens)
+        maxp = max(math.ceil(L / P) for L in lens)
+        slots = B * maxp + 1
+        perm = torch.randperm(slots, generator=gen)
+        pool = torch.randn(slots, 2, Hkv, P, D, generator=gen).to(dtype)
+        q = torch.randn(B, Hq, S, D, generator=gen).to(dtype)
+        page_table = np.zeros((B, maxp), np.int32)
+        for b in range(B):
+            for i in range(math.ceil(lens[b] / P)):
+                page_table[b, i] = int(perm[b * maxp + i])
+        mask = _chunk_mask(lens, S, T, dtype, s.get("pad"))
+        softcap = s.get("softcap")
+        outs, outs32 = [], []
+        for b in range(B):
+            for fp32 in (False, True):
+                plist = []
+                for i in range(math.ceil(lens[b] / P)):
+                    slot = int(page_table[b, i])
+                    k, v = pool[slot, 0].unsqueeze(0), pool[slot, 1].unsqueeze(0)
+                    if fp32:
+                        k, v = k.float(), v.float()
+                    plist.append(KVPage(page_id=i, layer_id=0, start_token=i * P,
+                                        used_tokens=min(P, lens[b] - i * P), capacity_tokens=P,
+                                        k_tensor=k, v_tensor=v, device=torch.device("cpu"),
+                                        state="CPU"))
+                qb = q[b:b + 1].float() if fp32 else q[b:b + 1]
+                o = perform_streaming_attention(qb, plist, scale=None,
+                                                attention_mask=mask[b:b + 1, :, :, :lens[b]],
+                                                softcap=softcap)
+                (outs32 if fp32 else outs).append(o[0])
+        pre = name + "/"
+        arrays[pre + "q"] = _bits(q)
+        arrays[pre + "pool"] = _bits(pool)
+        arrays[pre + "page_table"] = page_table
+        arrays[pre + "lens"] = np.array(lens, np.int32)
+        arrays[pre + "mask"] = mask.float().numpy()
+        arrays[pre + "out"] = _bits(torch.stack(outs))
+        arrays[pre + "out_fp32"] = torch.stack(outs32).numpy()
+        arrays[pre + "meta"] = np.array([Hq, Hkv, D, P, S, 0 if dtype == torch.bfloat16 else 1],
+                                        np.int64)
+        arrays[pre + "softcap"] = np.array([softcap or 0.0], np.float64)
+        names.append(name)
+    arrays["names"] = np.array(names)
+    np.savez_compressed(out_path, **arrays)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HELM_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["attention", "placement", "norm_rope", "prefill"],
+                    default=None)
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import helm  # noqa: F401  (fails loudly when the reference is absent)
     torch.manual_seed(0)
-    make_attention(args.ref, os.path.join(HERE, "attention.npz"))
-    make_placement(args.ref, os.path.join(HERE, "placement.json"))
-    make_norm_rope(args.ref, os.path.join(HERE, "norm_rope.npz"))
+    makers = {"attention": (make_attention, "attention.npz"),
+              "placement": (make_placement, "placement.json"),
+              "norm_rope": (make_norm_rope, "norm_rope.npz"),
+              "prefill": (make_prefill, "prefill.npz")}
+    for key, (fn, fname) in makers.items():
+        if args.only is None or args.only == key:
+            fn(args.ref, os.path.join(HERE, fname))
     print("golden fixtures written to", HERE)
 
 

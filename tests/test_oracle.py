@@ -155,3 +155,30 @@ def test_norm_rope_oracle_matches_hf(norm_rope_golden):
         c2, s2 = norm_rope.rope_tables(z[tag + "/pos"], q.shape[-1], float(z[tag + "/theta"][0]),
                                        dtype)
         assert np.mean(c2 == cos) > 0.99 and np.mean(s2 == sin) > 0.99, tag
+
+
+def prefill_oracle(case):
+    """A prefill chunk row by row: the oracle's streaming attention for one
+    query, with that query's mask row (kv_cache.py:469-555 treats every query
+    row independently)."""
+    q = _to_f32(case["q"], case["dtype"])            # [B, Hq, S, D]
+    B, Hq, S, D = q.shape
+    lens = case["lens"]
+    num_pages, page_used = oracle.dense_page_lists(lens, case["P"], case["page_table"].shape[1])
+    out = np.zeros((B, Hq, S, D), np.float32)
+    for s in range(S):
+        o, _ = oracle.paged_attention(
+            q[:, :, s], case["pool"], _pool_dtype(case), case["page_table"], num_pages,
+            page_used, num_kv_heads=case["Hkv"], page_size=case["P"], scale=D ** -0.5,
+            softcap=case["softcap_f"], mask=np.ascontiguousarray(case["mask"][:, 0, s]))
+        out[:, :, s] = o
+    return out
+
+
+def test_prefill_oracle_matches_reference(prefill_golden):
+    """Chunks of 30-100 queries under HELM's chunk mask (with key padding,
+    softcap, first chunk): the oracle equals the reference's fp32 output."""
+    for name, case in prefill_golden.items():
+        got = prefill_oracle(case)
+        ref = case["out_fp32"]
+        assert np.allclose(got, ref, atol=2e-5, rtol=2e-5), (name, np.abs(got - ref).max())

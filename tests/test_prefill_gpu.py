@@ -166,3 +166,27 @@ def test_prefill_output_layout_and_arguments(kernel):
     assert torch.equal(a, b)
     with pytest.raises(_capi.HelmError):
         _capi.paged_prefill_attention(*args, **{**kw, "page_size": 8})
+
+
+def test_prefill_kernel_matches_reference_golden(prefill_golden, kernel):
+    """Both kernels on the reference's own prefill-chunk outputs
+    (tests/golden/prefill.npz, produced by running perform_streaming_attention
+    with HELM's chunk masks): within the model-dtype tolerance of the
+    reference's fp32 result."""
+    dev = _cuda()
+    for name, c in prefill_golden.items():
+        dtype = torch.float16 if c["dtype"] == "float16" else torch.bfloat16
+        bits = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(dtype)  # noqa: E731
+        q, pool = bits(c["q"]), bits(c["pool"])
+        lens = [int(x) for x in c["lens"]]
+        mask = torch.from_numpy(c["mask"]).to(dtype)
+        out = _capi.paged_prefill_attention(
+            q.to(dev), pool.to(dev), torch.from_numpy(c["page_table"]).to(dev),
+            torch.tensor(lens, dtype=torch.int32, device=dev), num_kv_heads=c["Hkv"],
+            page_size=c["P"], scale=c["D"] ** -0.5, max_kv_len=max(lens), mask=mask.to(dev),
+            softcap=c["softcap_f"])
+        got = out.float().cpu().numpy()
+        ref = c["out_fp32"]
+        atol, rtol = TOL[dtype]
+        assert np.isfinite(got).all(), name
+        assert (np.abs(got - ref) <= atol + rtol * np.abs(ref)).all(), (name, np.abs(got - ref).max())
