@@ -114,3 +114,45 @@ def test_gloo_two_ranks_sequence_split_equals_full(tmp_path):
         lse = np.load(tmp_path / f"lse{r}.npy")
         np.testing.assert_allclose(out, full.reshape(out.shape), rtol=1e-5, atol=2e-6)
         np.testing.assert_allclose(lse, full_lse.reshape(-1), rtol=1e-6, atol=1e-5)
+
+
+def _leaving_worker(rank, world, port, out_dir):
+    """Both ranks finish one exchange; rank 1 then leaves between steps
+    (nothing in flight); rank 0's next exchange must end with an error within
+    the process group's timeout instead of waiting for good."""
+    import time
+    from datetime import timedelta
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    sp = SeqSplitAttention()
+    part = torch.full((6,), float(rank))
+    first = sp.exchange(part)
+    if rank == 1:
+        os._exit(0)  # departs without a further collective
+    t0 = time.time()
+    try:
+        sp.exchange(part)
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 - the kind of error is backend-specific
+        outcome = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.time() - t0:.2f}\n{first.tolist()}\n")
+    os._exit(0)
+
+
+def test_departed_rank_ends_the_next_exchange_with_an_error(tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank did not finish"
+    outcome, elapsed, first = (tmp_path / "rank0.txt").read_text().splitlines()
+    assert outcome.startswith("error"), outcome
+    assert float(elapsed) < 60
+    assert first == str([[0.0] * 6, [1.0] * 6])
