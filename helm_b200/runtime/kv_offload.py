@@ -29,8 +29,9 @@ import torch.nn.functional as F
 from .. import _capi
 from .kv_allocator import KVAllocator
 from .kv_cache import (KVCacheManager, _attend_lists, _layer_tables, _mask_2d,
-                       _prefill_over_pages, _stage_and_run, _stager_for,
-                       perform_streaming_attention)
+                       _prefill_over_pages, _stage_and_run, _stager_for)
+# re-exported: the reference module exposes it under this name (kv_offload.py:26)
+from .kv_cache import perform_streaming_attention  # noqa: F401
 
 
 @dataclass
