@@ -822,6 +822,8 @@ def run_model(args, rank: int, world: int, dev: torch.device):
                          "bytes_per_step": step_bytes, "weight_bytes": weight_bytes,
                          "kv_bytes_per_step_mean": kv_step,
                          "h2d_bytes_per_step": h2d_step, "h2d_link_gbs_measured": link,
+                         "h2d_gbs_achieved": h2d_step / (ms / 1e3) / 1e9,
+                         "h2d_frac_of_link": h2d_step / (ms / 1e3) / 1e9 / link,
                          "step_floor_ms": t_floor, "frac_of_floor": t_floor / ms,
                          "peak_source": peak_src},
             "e2e": {"value": Bq * (K + 1) / wall, "unit": "tok/s",
