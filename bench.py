@@ -450,14 +450,22 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
     the decode metric and a 131072-token prefill is not timed here).  Total
     work is fixed as N grows (strong scaling); time = max over ranks."""
     from helm_b200 import _capi
+    from helm_b200.runtime.seq_decode import SeqSplitDecodeModel
     from helm_b200.runtime.tp_decode import TPDecodeModel, synthetic_shard
     w = TP_WORKLOADS[args.workload]
     K = args.steps if args.steps_given else w["steps"]
     W = max(args.warmup, 3)
     Bq, ctx, arch = w["batch"], w["context"], w["arch"]
     e2e_steps = min(K, 32)
-    shard = synthetic_shard(arch, rank, world, w["dtype"], dev)
-    tp = TPDecodeModel(shard, batch=Bq, max_len=ctx + 3 + W + K + e2e_steps + 16, page_size=16)
+    seq = args.kv_split == "sequence"
+    if seq:   # the whole model on every rank (same seed), K/V split by token range
+        shard = synthetic_shard(arch, 0, 1, w["dtype"], dev)
+        tp = SeqSplitDecodeModel(shard, batch=Bq, context_len=ctx,
+                                 max_new=3 + W + K + e2e_steps + 16, page_size=16)
+    else:
+        shard = synthetic_shard(arch, rank, world, w["dtype"], dev)
+        tp = TPDecodeModel(shard, batch=Bq, max_len=ctx + 3 + W + K + e2e_steps + 16,
+                           page_size=16)
     try:
         tp.fill_kv(ctx)
         for _ in range(3):
@@ -503,6 +511,9 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
                      (lw.wqkv, lw.wo, lw.wg, lw.wu, lw.wd)) * shard.embed.element_size()
         wbytes += shard.lm_head.numel() * shard.lm_head.element_size() + Bq * arch["hidden"] * 2
         mean_ctx = ctx + 3 + W + K / 2
+        if seq:   # this rank's token range (the last rank also holds the new tokens)
+            a, b = tp.range
+            mean_ctx = (b - a) + ((3 + W + K / 2) if tp.tail else 0)
         kv_bytes = len(shard.layers) * Bq * mean_ctx * 2 * shard.hkv * shard.head_dim * 2
     finally:
         tp.close()
@@ -520,13 +531,19 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
             "data": "synthetic (random-init weight shards, N(0,1) K/V context)",
             "config": {"workload": f"{args.workload}: {w['name']} random-init, batch {Bq}, "
                                    f"{ctx}-token context (K/V filled synthetically), greedy "
-                                   f"decode, 16-token pages, tensor parallel x{world} (KV heads, "
-                                   f"q/k/v/gate/up rows, o/down columns, lm_head vocab)",
-                       "execution": "one CUDA graph replay per step; row-parallel projections "
-                                    "all-reduce over NVLink inside the GEMV kernel; greedy pick "
-                                    "by one NCCL all-gather",
+                                   f"decode, 16-token pages, " + (
+                                       f"K/V sequence-split x{world} (token ranges), weights "
+                                       f"replicated" if seq else
+                                       f"tensor parallel x{world} (KV heads, q/k/v/gate/up rows, "
+                                       f"o/down columns, lm_head vocab)"),
+                       "execution": ("one CUDA graph replay per step; per layer the partial "
+                                     "attention states (O, LSE) of the ranks are exchanged and "
+                                     "merged over NVLink by one peer-memory kernel" if seq else
+                                     "one CUDA graph replay per step; row-parallel projections "
+                                     "all-reduce over NVLink inside the GEMV kernel; greedy pick "
+                                     "by one NCCL all-gather"),
                        "l2": "weights + K/V per step exceed L2",
-                       "parallelism": f"tp{world}"},
+                       "parallelism": f"seq{world}" if seq else f"tp{world}"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": None,
                          "bytes_per_step_per_gpu": step_bytes, "weight_bytes_per_gpu": wbytes,
@@ -537,7 +554,7 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
                     "d2h_bytes_per_step": Bq * 8,
                     "note": "graph replay + per-step copy of the new tokens to pinned host "
                             "memory and a host sync (token streaming)"},
-            "gpu_launches": (7 * len(shard.layers) + 1) * K,
+            "gpu_launches": ((8 if seq and world > 1 else 7) * len(shard.layers) + 1) * K,
             "clocks": clocks.summary()}
     print(json.dumps(line), flush=True)
 
@@ -861,6 +878,10 @@ def main():
                     help="config1/config3: decode step as FusedDecodeStage or as HF modules")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="seqsplit128k: how partial states cross GPUs")
+    ap.add_argument("--kv-split", choices=["head", "sequence"], default="head",
+                    help="config4/config5 over N GPUs: tensor parallel with KV heads sharded "
+                         "(head), or the whole model on every rank with the K/V split by "
+                         "token range and partial states merged over NVLink (sequence)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seq-len", type=int, default=T,
                     help="tokens per sequence (profiling a smaller case only; for the "

@@ -156,3 +156,38 @@ def test_departed_rank_ends_the_next_exchange_with_an_error(tmp_path):
     assert outcome.startswith("error"), outcome
     assert float(elapsed) < 60
     assert first == str([[0.0] * 6, [1.0] * 6])
+
+
+def test_sequence_split_token_ownership():
+    """Model-level sequence split (runtime/seq_decode.py): for every position,
+    exactly one rank writes the token's K/V row (the one whose range holds it;
+    the last rank past the context), at its own next row; over all ranks a
+    query attends each of the pos + 1 tokens once."""
+    from helm_b200.runtime.seq_decode import token_rows
+    for T, P, world, extra in [(100, 16, 2, 20), (131072, 16, 8, 5), (40, 16, 4, 3), (64, 64, 2, 70)]:
+        ranges = split_ranges(T, P, world)
+        L, B = 2, 3
+        tabs, caps = [], []
+        for r, (a, b) in enumerate(ranges):
+            cap = (b - a) + (extra if r == world - 1 else 0)
+            maxp = max(1, -(-cap // P))
+            base = torch.arange(L * B, dtype=torch.int32).view(L, B, 1) * maxp
+            tabs.append(base + torch.arange(maxp, dtype=torch.int32))
+            caps.append(cap)
+        for p in list(range(0, min(T + extra, 300))) + list(range(T, T + extra)):
+            pos = torch.full((B,), p, dtype=torch.int32)
+            owners, total = [], torch.zeros(B, dtype=torch.int64)
+            for r, rng in enumerate(ranges):
+                rows, lens = token_rows(pos, rng, r == world - 1, caps[r], tabs[r], P)
+                total += lens.long()
+                if bool((rows >= 0).all()):
+                    owners.append(r)
+                    li = p - rng[0]
+                    want = tabs[r][:, :, li // P].long() * P + li % P
+                    assert torch.equal(rows, want)
+                else:
+                    assert bool((rows == -1).all())
+            assert len(owners) == 1, (T, world, p, owners)
+            a, b = ranges[owners[0]]
+            assert a <= p and (p < b or owners[0] == world - 1)
+            assert bool((total == p + 1).all()), (T, world, p, total)
