@@ -96,3 +96,44 @@ def test_two_ranks_sequence_split_match_hf(tmp_path, family):
     _assert_logits_close(eager[0], ref, ref32, dtype)
     assert torch.equal(eager[0], eager[1])       # every rank continues with the same state
     assert torch.equal(graph[0], eager[0]) and torch.equal(graph[1], eager[1])
+
+
+@pytest.mark.parametrize("family,dtype", [("qwen3", torch.bfloat16), ("llama", torch.float16)])
+def test_single_rank_equals_tensor_parallel_single_rank(family, dtype):
+    """On one GPU the sequence split issues the same kernels in the same order
+    as the tensor-parallel model: logits bit-identical, the prompt fed
+    eagerly, the forced steps replayed as a CUDA graph."""
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    from helm_b200 import _capi
+    from helm_b200.runtime.tp_decode import TPDecodeModel
+    dev = torch.device("cuda:0")
+    model = _tiny(family, dtype, dev)
+    prompt, forced = (t.to(dev) for t in _tokens())
+    w = shard_hf_model(model, 0, 1)
+    tp = TPDecodeModel(w, batch=1, max_len=S + N_STEPS + 8, page_size=16)
+    sd = SeqSplitDecodeModel(w, batch=1, context_len=S, max_new=N_STEPS + 8, page_size=16)
+    try:
+        sd.start(prompt[:, :1])
+        a, b = [], []
+        for t in range(S):
+            tp.ids.copy_(prompt[:, t:t + 1])
+            tp.step()
+            sd.ids.copy_(prompt[:, t:t + 1])
+            sd.step()
+        a.append(tp.full_logits())
+        b.append(sd.full_logits())
+        sd.capture()
+        for s in range(N_STEPS - 1):
+            tp.ids.copy_(forced[:, s:s + 1])
+            tp.step()
+            sd.ids.copy_(forced[:, s:s + 1])
+            sd.replay()
+            a.append(tp.full_logits())
+            b.append(sd.full_logits())
+        torch.cuda.synchronize()
+        assert _capi.device_status(dev) == 0
+        assert torch.equal(torch.stack(a), torch.stack(b))
+    finally:
+        tp.close()
+        sd.close()
