@@ -1,4 +1,5 @@
-"""Sequence-split decode (helm_b200.runtime.seq_decode) against HF on 2 GPUs.
+"""Sequence-split decode (helm_b200.runtime.seq_decode): against HF on 2 GPUs,
+and against the tensor-parallel model on one GPU.
 
 A tiny random-init Qwen3 (bf16) or Llama (fp16) model is replicated on both
 ranks; the prompt is consumed token by token (each token's K/V row lands on
