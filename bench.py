@@ -11,11 +11,14 @@ resident state in HBM (as in decode), the per-step inputs are q, the page
 table and the lengths.  512 MiB of K/V are read per step, so every step
 streams more than the 126 MB L2 (no flush needed).
 
-Prints one JSON line (rank 0).  `value` is achieved algorithmic HBM GB/s over
-all ranks (bytes of K/V + q + O + LSE + page table per step / device time).
-With N GPUs (torchrun) every rank runs its own config-2 problem (the path
-shards by sequence and KV head with no exchange): weak scaling, time = max
-over ranks.
+Prints one JSON line (rank 0).  `value` is achieved algorithmic HBM GB/s of
+the whole call (bytes of K/V + q + O + LSE + page table per step / device
+time).  With N GPUs (torchrun) the same call is split by sequence: every rank
+holds a page-aligned 1/N of each sequence's tokens in its own HBM, computes
+fp32 partial states, and one peer-memory kernel per call exchanges and merges
+them over NVLink (strong scaling; time = max over ranks).  The line also
+carries `model_decode`: decode tok/s of BASELINE configs[3] (Qwen3-14B,
+131072-token context, batch 1) tensor-parallel over the same N GPUs.
 """
 from __future__ import annotations
 
@@ -176,6 +179,13 @@ def cpu_baseline(q, pool, page_table, kv_lens, budget_s: float = 12.0, steps: in
             "times": times}
 
 
+def _config() -> dict:
+    """The workload, printed identically by both arms."""
+    return {"workload": WORKLOAD, "kv_bytes_per_step": KV_BYTES,
+            "algorithmic_bytes_per_step": ALG_BYTES,
+            "l2": "inputs larger than L2 (512 MiB K/V streamed per step), no flush"}
+
+
 def run_reference(args, rank: int):
     if rank != 0:
         return
@@ -186,151 +196,223 @@ def run_reference(args, rank: int):
     per = sum(res["times"]) / len(res["times"])
     line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "parallelism": "host threads"},
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "impl": "reference", "config": _config(),
+            "parallelism": f"host threads ({res['cores']}) of one node, rank 0 only",
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_b200(args, rank: int, world: int, dev: torch.device):
-    from helm_b200 import _capi
-    q, pool, pt, kl = make_inputs(0)
-    qd, pd, ptd, kld = q.to(dev), pool.to(dev), pt.to(dev), kl.to(dev)
-    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(B, HQ, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+def _split_inputs(rank: int, world: int, dev: torch.device):
+    """Rank `rank`'s share of the config-2 call split by sequence: tokens
+    [a, b) of every sequence (page-aligned, split_ranges), in a pool of its own
+    (the shard's pages at random slots), drawn on the device.  q is the same
+    on every rank."""
+    from helm_b200.runtime.seq_parallel import split_ranges
+    a, b = split_ranges(T, P, world)[rank]
+    npg = (b - a) // P
+    slots = B * npg + 64
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    pool = torch.randn(slots, 2, HKV, P, D, generator=g, device=dev).to(torch.bfloat16)
+    pt = torch.randperm(slots, generator=g, device=dev)[:B * npg].view(B, npg).to(torch.int32)
+    kl = torch.full((B,), b - a, dtype=torch.int32, device=dev)
+    q = torch.randn(B, HQ, D, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    return q, pool, pt, kl, b - a
 
-    def step():
-        _capi.paged_decode_attention(qd, pd, ptd, kld, num_kv_heads=HKV, page_size=P,
-                                     scale=D ** -0.5, out=out, lse=lse, max_kv_len_hint=T)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize(dev)
-    if _capi.device_status(dev) != 0:
-        raise RuntimeError("device status reported an error during warm-up")
-    # decode calls as a captured decode loop runs them: GRAPH_STEPS consecutive
-    # calls in one CUDA graph (each the decode kernel plus its PDL-dependent
-    # merge kernel; with decode overlap, the next call's decode kernel is
-    # placed while the previous merge runs -- its inputs are not written there)
-    gsteps = max(d for d in range(1, GRAPH_STEPS + 1) if args.steps % d == 0)
-    graph = torch.cuda.CUDAGraph()
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(stream)
-    with torch.cuda.stream(side), _capi.decode_overlap():
-        with torch.cuda.graph(graph, stream=side):
-            for _ in range(gsteps):
-                step()
-    stream.wait_stream(side)
-    graph.replay()
-    torch.cuda.synchronize(dev)
-
+def _timed(fn, steps: int, world: int, dev: torch.device, stream, clocks_soak: bool):
+    """Device time of `steps` calls of fn (CUDA events on `stream`, barrier and
+    synchronize on both sides), max over ranks; optional nvidia-smi sampling."""
     def barrier():
         if world > 1:
             torch.distributed.barrier()
-
-    # ---- device-resident timing (value) --------------------------------------
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_replays = args.steps // gsteps
     barrier()
     torch.cuda.synchronize(dev)
-    with ClockSampler(dev.index) as clocks:
-        # keep the GPU under the same load for ~0.6 s so that nvidia-smi sees it
-        t_soak = time.perf_counter()
-        while time.perf_counter() - t_soak < 0.6:
-            for _ in range(5):
-                graph.replay()
-            torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = None
+    with ClockSampler(dev.index) as sampler:
+        if clocks_soak:   # keep the GPU under the same load for ~0.6 s so nvidia-smi sees it
+            t_soak = time.perf_counter()
+            while time.perf_counter() - t_soak < 0.6:
+                fn(5)
+                torch.cuda.synchronize(dev)
         ev0.record(stream)
-        for i in range(n_replays):
-            graph.replay()
+        fn(steps)
         ev1.record(stream)
         torch.cuda.synchronize(dev)
+    clocks = sampler.summary()
     barrier()
-    elapsed_ms = ev0.elapsed_time(ev1)
-    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    mine = ev0.elapsed_time(ev1)
+    t = torch.tensor([mine], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    elapsed_ms = float(t.item())
-    value = ALG_BYTES * args.steps * world / (elapsed_ms / 1e3) / 1e9
+    return float(t.item()), mine, clocks
 
-    # ---- end to end through the public API, host buffers ---------------------
-    q_host = q.clone().pin_memory()
-    pt_host = pt.clone().pin_memory()
-    kl_host = kl.clone().pin_memory()
-    out_host = torch.empty(B, HQ, D, dtype=torch.bfloat16).pin_memory()
-    lse_host = torch.empty(B, HQ, dtype=torch.float32).pin_memory()
-    h2d = q_host.numel() * 2 + pt_host.numel() * 4 + kl_host.numel() * 4
-    d2h = out_host.numel() * 2 + lse_host.numel() * 4
 
-    def e2e_step():
-        qd.copy_(q_host, non_blocking=True)
-        ptd.copy_(pt_host, non_blocking=True)
-        kld.copy_(kl_host, non_blocking=True)
-        step()
-        out_host.copy_(out, non_blocking=True)
-        lse_host.copy_(lse, non_blocking=True)
-
-    for _ in range(3):
-        e2e_step()
-    barrier()
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    t2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+def run_b200(args, rank: int, world: int, dev: torch.device):
+    """Config 2 on `world` GPUs.  N = 1: the whole call on one GPU.  N > 1: the
+    same call split by sequence -- every rank streams its token range of all
+    four sequences from its own HBM into fp32 partial states, and one
+    peer-memory kernel per call exchanges and merges them over NVLink, so
+    every rank ends with the full output (strong scaling, total work fixed)."""
+    from helm_b200 import _capi
+    stream = torch.cuda.current_stream(dev)
+    if world == 1:
+        q, pool, pt, kl = make_inputs(0)
+        qd, pd, ptd, kld = q.to(dev), pool.to(dev), pt.to(dev), kl.to(dev)
+        t_rank = T
+    else:
+        q, pd, ptd, kld, t_rank = _split_inputs(rank, world, dev)
+        qd = q.to(dev)
+        pt = ptd.cpu()
+        kl = kld.cpu()
+    out = torch.empty(B, HQ, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, HQ, dtype=torch.float32, device=dev)
+    px = None
     if world > 1:
-        torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
-    e2e_value = ALG_BYTES * args.steps * world / (float(t2.item()) / 1e3) / 1e9
-    # the end-to-end result must equal the device-resident one
-    torch.cuda.synchronize(dev)
-    if not torch.equal(out_host.to(dev), out):
-        raise RuntimeError("end-to-end output differs from the device-resident output")
+        from helm_b200.runtime.seq_parallel import PeerExchange
+        px = PeerExchange(B * HQ, D, dev)
+        part = torch.empty(B * HQ * (D + 1), dtype=torch.float32, device=dev)
+        o_part, lse_part = part[:B * HQ * D].view(B, HQ, D), part[B * HQ * D:].view(B, HQ)
+
+    def step(qx=None, ptx=None, klx=None, outx=None, lsex=None):
+        qx = qd if qx is None else qx
+        ptx = ptd if ptx is None else ptx
+        klx = kld if klx is None else klx
+        outx = out if outx is None else outx
+        lsex = lse if lsex is None else lsex
+        if px is None:
+            _capi.paged_decode_attention(qx, pd, ptx, klx, num_kv_heads=HKV, page_size=P,
+                                         scale=D ** -0.5, out=outx, lse=lsex,
+                                         max_kv_len_hint=t_rank)
+            return
+        _capi.paged_decode_attention(qx, pd, ptx, klx, num_kv_heads=HKV, page_size=P,
+                                     scale=D ** -0.5, out=o_part, lse=lse_part,
+                                     max_kv_len_hint=t_rank)
+        px.merge(o_part.view(B * HQ, D), lse_part.view(B * HQ), outx.view(B * HQ, D),
+                 lsex.view(B * HQ))
+
+    try:
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize(dev)
+        if _capi.device_status(dev) != 0:
+            raise RuntimeError("device status reported an error during warm-up")
+        # decode calls as a captured decode loop runs them: GRAPH_STEPS consecutive
+        # calls in one CUDA graph (each the decode kernel plus its PDL-dependent
+        # merge kernel, or at N > 1 the peer exchange-merge; with decode overlap,
+        # the next call's decode kernel is placed while the previous one finishes
+        # -- its inputs are not written there)
+        gsteps = max(d for d in range(1, GRAPH_STEPS + 1) if args.steps % d == 0)
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side), _capi.decode_overlap():
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(gsteps):
+                    step()
+        stream.wait_stream(side)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+
+        def replays(n_steps):
+            for _ in range(max(1, n_steps // gsteps)):
+                graph.replay()
+
+        elapsed_ms, mine_ms, clocks = _timed(replays, args.steps, world, dev, stream, True)
+        value = ALG_BYTES * args.steps / (elapsed_ms / 1e3) / 1e9
+
+        # ---- end to end through the public API, host buffers ---------------------
+        # per step: one pinned H2D copy of the packed inputs (q, page table,
+        # lengths) and one D2H copy of the packed results (O, LSE)
+        n_q, n_pt, n_kl = qd.numel() * 2, ptd.numel() * 4, kld.numel() * 4
+        n_in = n_q + n_pt + n_kl
+        host_in = torch.empty(n_in, dtype=torch.uint8).pin_memory()
+        host_in[:n_q].view(torch.bfloat16).copy_(q.reshape(-1))
+        host_in[n_q:n_q + n_pt].view(torch.int32).copy_(pt.reshape(-1))
+        host_in[n_q + n_pt:].view(torch.int32).copy_(kl.reshape(-1))
+        dev_in = torch.empty(n_in, dtype=torch.uint8, device=dev)
+        q_in = dev_in[:n_q].view(torch.bfloat16).view(B, HQ, D)
+        pt_in = dev_in[n_q:n_q + n_pt].view(torch.int32).view(ptd.shape)
+        kl_in = dev_in[n_q + n_pt:].view(torch.int32)
+        n_o, n_l = out.numel() * 2, lse.numel() * 4
+        dev_res = torch.empty(n_o + n_l, dtype=torch.uint8, device=dev)
+        out_res = dev_res[:n_o].view(torch.bfloat16).view(B, HQ, D)
+        lse_res = dev_res[n_o:].view(torch.float32).view(B, HQ)
+        host_res = torch.empty(n_o + n_l, dtype=torch.uint8).pin_memory()
+
+        def e2e(n_steps):
+            for _ in range(n_steps):
+                dev_in.copy_(host_in, non_blocking=True)
+                step(q_in, pt_in, kl_in, out_res, lse_res)
+                host_res.copy_(dev_res, non_blocking=True)
+
+        e2e(3)
+        e2e_ms, _, _ = _timed(e2e, args.steps, world, dev, stream, False)
+        e2e_value = ALG_BYTES * args.steps / (e2e_ms / 1e3) / 1e9
+        # the end-to-end result must equal the device-resident one
+        torch.cuda.synchronize(dev)
+        if not torch.equal(host_res[:n_o].view(torch.bfloat16).view(B, HQ, D).to(dev), out):
+            raise RuntimeError("end-to-end output differs from the device-resident output")
+        del graph
+        status = _capi.device_status(dev)
+    finally:
+        if px is not None:
+            px.close()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+
+    model = None
+    if not args.no_model_block:
+        model = _model_block(_tp_decode("config4", args, rank, world, dev, steps=32,
+                                        warmup=3), world)
 
     if rank != 0:
         return
     peak, peak_src = _peaks()
-    avg_launch_ms = ev0.elapsed_time(ev1) / args.steps   # this rank, kernels of one call
-    achieved = ALG_BYTES / (avg_launch_ms / 1e3) / 1e9
+    avg_launch_ms = mine_ms / args.steps   # this rank, kernels of one call
+    rank_bytes = ALG_BYTES if world == 1 else \
+        (B * t_rank * HKV * D * 2 * 2 + B * HQ * D * 2 + B * HQ * (D + 1) * 4 + ptd.numel() * 4
+         + B * 4)
+    achieved = rank_bytes / (avg_launch_ms / 1e3) / 1e9
     traffic = None
     tpath = os.path.join(REPO, "profiles", "paged_decode_config2_traffic.json")
-    if os.path.exists(tpath):
+    if world == 1 and os.path.exists(tpath):
         with open(tpath) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": WORKLOAD, "kv_bytes_per_step": KV_BYTES,
-                   "algorithmic_bytes_per_step": ALG_BYTES,
-                   "l2": "inputs larger than L2 (512 MiB K/V streamed per step), no flush",
-                   "parallelism": f"replicas x{world} (shard by sequence/KV head, no exchange)",
-                   "decode_attention_calls_per_s": 1e3 / (elapsed_ms / args.steps) * world,
-                   "sequences_decoded_per_s_one_layer":
-                       B * 1e3 / (elapsed_ms / args.steps) * world},
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": _config(),
+        "parallelism": ("one GPU" if world == 1 else
+                        f"sequence split x{world}: {t_rank} tokens of each sequence per GPU, "
+                        "fp32 (O, LSE) exchanged and merged over NVLink by one peer-memory "
+                        "kernel per call"),
+        "decode_attention_calls_per_s": 1e3 / (elapsed_ms / args.steps),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "paged_decode_kernel + merge_split_pairs_kernel (PDL dependent); "
-                               "achieved = algorithmic bytes / time of the whole step",
+                     "kernel": ("paged_decode_kernel + merge_split_pairs_kernel (PDL dependent)"
+                                if world == 1 else
+                                "paged_decode_kernel (fp32 partial) + seq_exchange_merge_kernel")
+                               + "; achieved = this GPU's algorithmic bytes / time of the "
+                                 "whole step",
                      "peak_source": peak_src,
                      "clock_note": "clocks sampled over a 0.6 s soak at the same load "
                                    "immediately before and during the timed region"},
-        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": n_in,
+                "d2h_bytes_per_step": n_o + n_l,
+                "note": "one packed pinned H2D copy (q, page table, lengths) and one packed "
+                        "D2H copy (O, LSE) per call, eager launches through the C-ABI wrapper"},
         "gpu_launches": 2 * args.steps,
         "execution": f"value: CUDA graphs of {gsteps} consecutive decode calls (decode "
-                     "overlap on), replayed; e2e: eager calls through the C-ABI wrapper with "
-                     "host copies",
-        "clocks": clocks.summary(),
+                     "overlap on), replayed",
+        "clocks": clocks,
     }
+    if model is not None:
+        line["model_decode"] = model
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline(q, pool, pt, kl)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -443,21 +525,21 @@ TP_WORKLOADS = {
 }
 
 
-def run_tp(args, rank: int, world: int, dev: torch.device):
+def _tp_decode(name: str, args, rank: int, world: int, dev: torch.device, steps: int,
+               warmup: int, seq: bool = False, profile_step: bool = False) -> dict:
     """Decode tok/s of a tensor-parallel model over `world` GPUs (BASELINE
     configs[3] / configs[4]).  Random-init weights drawn per shard; the
     context's K/V pages are filled with N(0,1) values (prefill is not part of
     the decode metric and a 131072-token prefill is not timed here).  Total
-    work is fixed as N grows (strong scaling); time = max over ranks."""
+    work is fixed as N grows (strong scaling); time = max over ranks.  Returns
+    the measurements (every rank)."""
     from helm_b200 import _capi
     from helm_b200.runtime.seq_decode import SeqSplitDecodeModel
     from helm_b200.runtime.tp_decode import TPDecodeModel, synthetic_shard
-    w = TP_WORKLOADS[args.workload]
-    K = args.steps if args.steps_given else w["steps"]
-    W = max(args.warmup, 3)
+    w = TP_WORKLOADS[name]
+    K, W = steps, max(warmup, 3)
     Bq, ctx, arch = w["batch"], w["context"], w["arch"]
     e2e_steps = min(K, 32)
-    seq = args.kv_split == "sequence"
     if seq:   # the whole model on every rank (same seed), K/V split by token range
         shard = synthetic_shard(arch, 0, 1, w["dtype"], dev)
         tp = SeqSplitDecodeModel(shard, batch=Bq, context_len=ctx,
@@ -474,17 +556,13 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
         for _ in range(W):
             tp.replay()
         torch.cuda.synchronize(dev)
-        if world > 1:
-            torch.distributed.barrier()
-        stream = torch.cuda.current_stream(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with ClockSampler(dev.index) as clocks:
-            e0.record(stream)
-            for _ in range(K):
+
+        def replays(n):
+            for _ in range(n):
                 tp.replay()
-            e1.record(stream)
-            torch.cuda.synchronize(dev)
-        ms_rank = e0.elapsed_time(e1) / K
+        ms_total, _, clocks = _timed(replays, K, world, dev, torch.cuda.current_stream(dev),
+                                     False)
+        ms = ms_total / K
         # end to end: every step's tokens read back to pinned host memory (streaming)
         host_tok = torch.empty(Bq, 1, dtype=torch.long).pin_memory()
         if world > 1:
@@ -495,11 +573,11 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
             host_tok.copy_(tp.ids, non_blocking=True)
             torch.cuda.current_stream(dev).synchronize()
         e2e_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
-        t = torch.tensor([ms_rank, e2e_ms], dtype=torch.float64, device=dev)
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         if world > 1:
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, e2e_ms = float(t[0]), float(t[1])
-        if args.profile_step:   # one eager step for `ncu --profile-from-start off`
+        e2e_ms = float(t[0])
+        if profile_step:   # one eager step for `ncu --profile-from-start off`
             torch.cuda.synchronize(dev)
             torch.cuda.profiler.start()
             tp.step()
@@ -515,27 +593,43 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
             a, b = tp.range
             mean_ctx = (b - a) + ((3 + W + K / 2) if tp.tail else 0)
         kv_bytes = len(shard.layers) * Bq * mean_ctx * 2 * shard.hkv * shard.head_dim * 2
+        n_layers = len(shard.layers)
     finally:
         tp.close()
+        del tp, shard
+        torch.cuda.empty_cache()
     if status != 0:
         raise RuntimeError(f"device status {status}")
-    if rank != 0:
-        return
     hbm, peak_src = _peaks()
     step_bytes = wbytes + kv_bytes
     achieved = step_bytes / (ms / 1e3) / 1e9
-    line = {"metric": METRIC, "value": Bq / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
-            "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+    return dict(w=w, K=K, W=W, Bq=Bq, ctx=ctx, ms=ms, e2e_ms=e2e_ms, clocks=clocks,
+                wbytes=wbytes, kv_bytes=kv_bytes, step_bytes=step_bytes, achieved=achieved,
+                hbm=hbm, peak_src=peak_src, n_layers=n_layers,
+                tok_s=Bq / (ms / 1e3), roofline_tok_s=Bq / (step_bytes / (hbm * 1e9)),
+                workload=(f"{name}: {w['name']} random-init, batch {Bq}, {ctx}-token context "
+                          f"(K/V filled synthetically), greedy decode, 16-token pages, " + (
+                              f"K/V sequence-split x{world} (token ranges), weights replicated"
+                              if seq else
+                              f"tensor parallel x{world} (KV heads, q/k/v/gate/up rows, "
+                              f"o/down columns, lm_head vocab)")))
+
+
+def run_tp(args, rank: int, world: int, dev: torch.device):
+    w = TP_WORKLOADS[args.workload]
+    seq = args.kv_split == "sequence"
+    r = _tp_decode(args.workload, args, rank, world, dev,
+                   args.steps if args.steps_given else w["steps"], args.warmup, seq=seq,
+                   profile_step=args.profile_step)
+    if rank != 0:
+        return
+    K, Bq = r["K"], r["Bq"]
+    line = {"metric": METRIC, "value": r["tok_s"], "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": r["W"], "ms_per_step": r["ms"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16" if w["dtype"] == torch.bfloat16 else "fp16",
             "data": "synthetic (random-init weight shards, N(0,1) K/V context)",
-            "config": {"workload": f"{args.workload}: {w['name']} random-init, batch {Bq}, "
-                                   f"{ctx}-token context (K/V filled synthetically), greedy "
-                                   f"decode, 16-token pages, " + (
-                                       f"K/V sequence-split x{world} (token ranges), weights "
-                                       f"replicated" if seq else
-                                       f"tensor parallel x{world} (KV heads, q/k/v/gate/up rows, "
-                                       f"o/down columns, lm_head vocab)"),
+            "config": {"workload": r["workload"],
                        "execution": ("one CUDA graph replay per step; per layer the partial "
                                      "attention states (O, LSE) of the ranks are exchanged and "
                                      "merged over NVLink by one peer-memory kernel" if seq else
@@ -544,19 +638,29 @@ def run_tp(args, rank: int, world: int, dev: torch.device):
                                      "by one NCCL all-gather"),
                        "l2": "weights + K/V per step exceed L2",
                        "parallelism": f"seq{world}" if seq else f"tp{world}"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
-                         "bytes_per_step_per_gpu": step_bytes, "weight_bytes_per_gpu": wbytes,
-                         "kv_bytes_per_step_per_gpu": kv_bytes,
-                         "roofline_tok_s": Bq / (step_bytes / (hbm * 1e9)),
-                         "peak_source": peak_src},
-            "e2e": {"value": Bq / (e2e_ms / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+            "roofline": {"bound": "hbm", "achieved": r["achieved"], "peak": r["hbm"],
+                         "unit": "GB/s", "frac": r["achieved"] / r["hbm"], "traffic": None,
+                         "bytes_per_step_per_gpu": r["step_bytes"],
+                         "weight_bytes_per_gpu": r["wbytes"],
+                         "kv_bytes_per_step_per_gpu": r["kv_bytes"],
+                         "roofline_tok_s": r["roofline_tok_s"], "peak_source": r["peak_src"]},
+            "e2e": {"value": Bq / (r["e2e_ms"] / 1e3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": Bq * 8,
                     "note": "graph replay + per-step copy of the new tokens to pinned host "
                             "memory and a host sync (token streaming)"},
-            "gpu_launches": ((8 if seq and world > 1 else 7) * len(shard.layers) + 1) * K,
-            "clocks": clocks.summary()}
+            "gpu_launches": ((8 if seq and world > 1 else 7) * r["n_layers"] + 1) * K,
+            "clocks": r["clocks"]}
     print(json.dumps(line), flush=True)
+
+
+def _model_block(r: dict, world: int) -> dict:
+    """The config-4 decode summary carried in the default bench line."""
+    return {"metric": "decode tok/s", "workload": r["workload"], "n_gpus": world,
+            "tok_s": r["tok_s"], "ms_per_step": r["ms"], "steps": r["K"],
+            "roofline_tok_s_per_gpu_bytes": r["roofline_tok_s"],
+            "roofline_frac": r["achieved"] / r["hbm"], "achieved_gbs_per_gpu": r["achieved"],
+            "bytes_per_step_per_gpu": r["step_bytes"],
+            "e2e_tok_s": r["Bq"] / (r["e2e_ms"] / 1e3), "clocks": r["clocks"]}
 
 
 GEMV_SHAPES = {  # one Qwen3-14B layer (configs[3]) at batch 1: (rows, input width, SwiGLU)
@@ -883,6 +987,8 @@ def main():
                          "(head), or the whole model on every rank with the K/V split by "
                          "token range and partial states merged over NVLink (sequence)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model-block", action="store_true",
+                    help="default workload: skip the config-4 model-decode block")
     ap.add_argument("--seq-len", type=int, default=T,
                     help="tokens per sequence (profiling a smaller case only; for the "
                          "prefill workload, the cached tokens, default 131072)")

@@ -53,7 +53,14 @@ size_t gemv_smem_bytes(int64_t k) {
 }
 
 constexpr int kArMaxRanks = 8;
-constexpr int64_t kArHeaderBytes = 8192;  // uint32 epoch per CTA (<= 2048 CTAs)
+// Exchange buffer: header {uint32 call epoch, uint32 CTAs done} (padded to
+// 256 bytes), then words {fp32 value, epoch} [2 parities][world][n][kArBatch].
+// The epoch belongs to the call, not to a CTA, and the batch stride is fixed:
+// consecutive calls with different grids or batch slices then use disjoint
+// parity halves for every (row, batch row) word, so a rank one call ahead
+// never overwrites a word a slower rank has still to read.
+constexpr int64_t kArHeaderBytes = 256;
+constexpr int kArBatch = 16;  // the widest batch one call takes
 
 struct GemvArgs {
   unsigned char* bufs[kArMaxRanks];  // all-reduce exchange buffers of every rank
@@ -118,6 +125,26 @@ __device__ __forceinline__ uint2 ld_volatile_u2(const uint2* p) {
   return v;
 }
 
+// Epoch of this call: one more than the previous call's, read after
+// griddepcontrol.wait (every earlier kernel of the stream has completed).
+__device__ __forceinline__ uint32_t ar_read_epoch(const GemvArgs& a) {
+  const volatile uint32_t* hdr = reinterpret_cast<const volatile uint32_t*>(a.bufs[a.rank]);
+  return hdr[0] + 1u;
+}
+
+// The last CTA of the call to get here stores the call's epoch (and re-arms
+// the done counter) for the next call; a timed-out call advances it too, and
+// the buffers of all ranks are then re-zeroed before the next use.
+__device__ __forceinline__ void ar_finish_call(const GemvArgs& a, uint32_t e) {
+  uint32_t* hdr = reinterpret_cast<uint32_t*>(a.bufs[a.rank]);
+  __threadfence();
+  if (atomicAdd(hdr + 1, 1u) == gridDim.x - 1) {
+    hdr[1] = 0u;
+    hdr[0] = e;
+    __threadfence();
+  }
+}
+
 __device__ __forceinline__ uint64_t gemv_timer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -135,8 +162,8 @@ __device__ __forceinline__ uint64_t gemv_timer_ns() {
 __device__ __forceinline__ void ar_push(const GemvArgs& a, uint32_t e, int64_t row, int b,
                                         float part) {
   const int par = static_cast<int>(e & 1u);
-  const int64_t slot_words = a.n * a.batch;
-  const int64_t off = row * a.batch + b;
+  const int64_t slot_words = a.n * kArBatch;
+  const int64_t off = row * kArBatch + b;
   for (int p = 0; p < a.world; ++p) {
     uint2* dst = reinterpret_cast<uint2*>(a.bufs[p] + kArHeaderBytes) +
                  (static_cast<int64_t>(par) * a.world + a.rank) * slot_words + off;
@@ -147,8 +174,8 @@ __device__ __forceinline__ void ar_push(const GemvArgs& a, uint32_t e, int64_t r
 __device__ __forceinline__ bool ar_poll(const GemvArgs& a, uint32_t e, int64_t row, int b,
                                         uint64_t t0, float& sum) {
   const int par = static_cast<int>(e & 1u);
-  const int64_t slot_words = a.n * a.batch;
-  const int64_t off = row * a.batch + b;
+  const int64_t slot_words = a.n * kArBatch;
+  const int64_t off = row * kArBatch + b;
   const uint2* own = reinterpret_cast<const uint2*>(a.bufs[a.rank] + kArHeaderBytes) +
                      static_cast<int64_t>(par) * a.world * slot_words + off;
   uint2 w[kArMaxRanks];
@@ -282,12 +309,12 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
 #pragma unroll 1
   for (int i = 0; i < kDepth - 1; ++i) issue_next();
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // all-reduce: this CTA's epoch (one counter per CTA index, same rows on
-  // every rank), advanced at the end of the call
+  // all-reduce: the call's epoch (the previous call on this stream has
+  // completed and advanced it), advanced by the last CTA to finish
   __shared__ uint32_t s_epoch;
   __shared__ int s_ar_ok;
   if (AR && threadIdx.x == 0) {
-    s_epoch = reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] + 1u;
+    s_epoch = ar_read_epoch(a);
     s_ar_ok = 1;
   }
 
@@ -443,7 +470,7 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
   }
   if (AR) {
     __syncthreads();
-    if (threadIdx.x == 0 && s_ar_ok) reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] = s_epoch;
+    if (threadIdx.x == 0) ar_finish_call(a, s_epoch);
   }
 }
 
@@ -517,7 +544,7 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
   __shared__ uint32_t s_epoch;
   __shared__ int s_ar_ok;
   if (AR && threadIdx.x == 0) {
-    s_epoch = reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] + 1u;
+    s_epoch = ar_read_epoch(a);
     s_ar_ok = 1;
   }
   for (int b = 0; b < NB; ++b) {
@@ -655,7 +682,7 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
   }
   if (AR) {
     __syncthreads();
-    if (threadIdx.x == 0 && s_ar_ok) reinterpret_cast<uint32_t*>(a.bufs[a.rank])[blockIdx.x] = s_epoch;
+    if (threadIdx.x == 0) ar_finish_call(a, s_epoch);
   }
 }
 
@@ -715,7 +742,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
   const int rpi = (kWarps / ks) * unit;
   const int64_t want = (a.n + rpi - 1) / rpi;
   const int grid = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms_current_device()) * fit));
-  if (AR && grid * 4 > kArHeaderBytes) return HELM_ERR_UNSUPPORTED;
+  if (AR && a.batch > kArBatch) return HELM_ERR_UNSUPPORTED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(GemvShape<NB>::kThreads);
@@ -778,7 +805,8 @@ extern "C" int helm_decode_gemv_allreduce(void* const* bufs, int rank, int world
 
 extern "C" int64_t helm_decode_gemv_allreduce_bytes(int64_t n, int batch, int world) {
   if (n <= 0 || batch <= 0 || world < 1 || world > helm::kArMaxRanks) return -1;
-  return helm::kArHeaderBytes + 2 * static_cast<int64_t>(world) * n * batch * 8;
+  if (batch > helm::kArBatch) return -1;
+  return helm::kArHeaderBytes + 2 * static_cast<int64_t>(world) * n * helm::kArBatch * 8;
 }
 
 extern "C" int helm_decode_gemv(const void* x, int64_t x_stride, const void* norm_w, float eps,

@@ -950,7 +950,7 @@ int64_t paged_decode_slots(int batch, int num_kv_heads) {
          static_cast<int64_t>(batch) * num_kv_heads;
 }
 
-// Workspace: reserved [B*Hkv] int32 (kept zero) | partial O [slots][G][D] fp32 |
+// Workspace: reserved [B*Hkv] int32 | partial O [slots][G][D] fp32 |
 // partial (m, l) [slots][G][2] fp32, each region 256-byte aligned.  The
 // reserved region (the first roundup(4*B*Hkv, 256) bytes) is neither read
 // nor written.

@@ -23,6 +23,8 @@
 //  * Nothing in the array has to start at zero: every value a call reads was
 //    written earlier in the same call, so a call never depends on what an
 //    earlier (or an abandoned) call left behind.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace helm {
@@ -34,7 +36,10 @@ constexpr int64_t kNoAllocScratchBytes = int64_t(8) << 20;
 // device array: the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-void* g_noalloc_scratch_addr[64] = {nullptr};  // per device, filled on first use
+// Per device, filled on first use.  Two host threads making the first call on
+// one device at the same time both look the address up and store the same
+// value; the atomics make that well defined.
+std::atomic<void*> g_noalloc_scratch_addr[64];
 
 }  // namespace
 }  // namespace helm
@@ -61,14 +66,14 @@ extern "C" int helm_paged_decode_attention_noalloc(
     return HELM_ERR_CUDA;
   }
   if (dev < 0 || dev >= 64) return HELM_ERR_UNSUPPORTED;
-  void* scratch = g_noalloc_scratch_addr[dev];
+  void* scratch = g_noalloc_scratch_addr[dev].load(std::memory_order_acquire);
   if (scratch == nullptr) {  // one-time set-up for this device
     e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
     if (e != cudaSuccess) {
       set_last_cuda_error(e);
       return HELM_ERR_CUDA;
     }
-    g_noalloc_scratch_addr[dev] = scratch;
+    g_noalloc_scratch_addr[dev].store(scratch, std::memory_order_release);
   }
   return helm_paged_decode_attention(
       q, q_stride_b, q_stride_h, kv_pool, pool_pages, page_table, pt_stride_b, max_pages, kv_lens,

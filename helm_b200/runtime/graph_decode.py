@@ -321,6 +321,8 @@ class GraphDecoder:
             if host.capacity - host.next_slot < need:
                 host.reserve_capacity(need)
         logits0 = loop.prefill(input_ids)
+        for kvcm in self.mgr.kvcms:   # the replayed step reads pages only: no all-GPU window
+            kvcm.migrate_contiguous_to_pages()
         self.ctx = _GraphContext(self.mgr, B, self.Hq, self.D, self.L, self.max_len, self.dtype,
                                  self.dev)
         self.ids = torch.argmax(logits0, dim=-1, keepdim=True)

@@ -47,6 +47,7 @@ class PagePool:
         self.pending_release: list[int] = []  # released once deferred copies are issued
         self.pages: dict[int, object] = {}    # slot -> page owning it (for re-pointing)
         self.staging: list[int] = []          # slots reserved for cold-page staging
+        self.window: set = set()              # slots reserved as all-GPU decode windows
         self.page_bytes = 2 * num_kv_heads * page_size * head_dim * \
             torch.tensor([], dtype=dtype).element_size()
         self._arenas: dict = {}               # key -> (next slot, end) (host tier)
@@ -129,7 +130,7 @@ class PagePool:
             return True
         owner = self.pages.get(s)
         if owner is None:
-            return s not in self.staging
+            return s not in self.staging and s not in self.window
         return owner is page or owner.state == "FREE"
 
     def _carve(self, page) -> int:
@@ -170,6 +171,21 @@ class PagePool:
     def flush_pending(self) -> None:
         self.free_slots.extend(self.pending_release)
         self.pending_release.clear()
+
+    def reserve_window(self, n: int) -> list[int]:
+        """n fresh slots reserved for a manager's decode window (never given to
+        pages until release_window).  Raises when the pool cannot grow."""
+        self.reserve_capacity(n)
+        slots = list(range(self.next_slot, self.next_slot + n))
+        self.next_slot += n
+        self.window.update(slots)
+        return slots
+
+    def release_window(self, slots) -> None:
+        for s in slots:
+            if s in self.window:
+                self.window.discard(s)
+                self.free_slots.append(s)
 
     def staging_slots(self, n: int) -> list[int]:
         """At least n slots reserved for cold-page staging (never given to pages)."""

@@ -542,8 +542,9 @@ class KVCacheManager:
         self._n_evictable = 0
         self._rank_counter = 0
         self._fingerprint: tuple = ()
-        self.cont_K: dict = {}
-        self.cont_V: dict = {}
+        # all-GPU window (build_contiguous): layer -> reserved device-pool slots
+        self._window: dict = {}
+        self._window_pool = None
         self.cont_capacity: int = 0
         self.cont_num_layers: int = 0
         self.cont_seq_len: int = 0
@@ -814,76 +815,180 @@ class KVCacheManager:
                 return False
         return True
 
-    # -- contiguous buffers (kv_cache.py:269-354) --------------------------------
-    # The paged kernel reads pages at full bandwidth, so the decode path here
-    # always appends to and reads from pages; these buffers are kept for API
-    # compatibility only.
+    # -- all-GPU window: the reference's contiguous buffers (kv_cache.py:269-354) --
+    # For all-GPU plans the reference keeps a second, dense [1, H, capacity, D]
+    # copy of every layer's K/V (its page path re-concatenates pages on every
+    # step).  Here the paged kernel reads pages at full bandwidth, so the
+    # capacity becomes a reservation of device-pool slots per layer, the
+    # "window": decode tokens of the window phase are written into it (one
+    # fused-append row each) and attention reads the layer's pages plus the
+    # window through one page table.  Nothing is held twice and prefill is not
+    # copied again.  The observable contract is the reference's:
+    # use_contiguous, cont_capacity, cont_seq_len and cont_prefill_len change
+    # under the same rules, decode tokens stay out of the page lists until
+    # cont_seq_len reaches the capacity, and migrate_contiguous_to_pages then
+    # appends them as append_prefill does (same page ids, start/used tokens
+    # and residency decisions).
     def build_contiguous(self, num_layers: int, num_kv_heads: int, head_dim: int,
                          capacity: int, device: torch.device, dtype: torch.dtype) -> bool:
+        """Reserves ceil(capacity / page_size) pool slots per layer on `device`;
+        when the pool cannot grow that far, retries with half the capacity
+        down to min(capacity, 1024) tokens.  False if every attempt fails."""
+        a = self.allocator
+        if (num_kv_heads, head_dim, dtype) != (a.num_kv_heads, a.head_dim, a.dtype):
+            raise ValueError("build_contiguous: geometry differs from the allocator's pages")
+        P = a.page_size
+        pool = a.pool_for(device)
         cap = capacity
         floor = max(1, min(capacity, 1024))
         while cap >= floor:
+            self._release_window()
+            per_layer = -(-cap // P)
             try:
-                self.cont_K.clear()
-                self.cont_V.clear()
-                for lid in range(num_layers):
-                    self.cont_K[lid] = torch.zeros(1, num_kv_heads, cap, head_dim, device=device,
-                                                   dtype=dtype)
-                    self.cont_V[lid] = torch.zeros(1, num_kv_heads, cap, head_dim, device=device,
-                                                   dtype=dtype)
-                self.cont_capacity = cap
-                self.cont_num_layers = num_layers
-                self.use_contiguous = True
-                return True
+                slots = pool.reserve_window(per_layer * num_layers)
             except (torch.cuda.OutOfMemoryError, RuntimeError):
-                self.cont_K.clear()
-                self.cont_V.clear()
-                if torch.device(device).type == "cuda":
+                if pool.device.type == "cuda":
                     torch.cuda.empty_cache()
                 cap //= 2
+                continue
+            self._window = {lid: slots[lid * per_layer:(lid + 1) * per_layer]
+                            for lid in range(num_layers)}
+            self._window_pool = pool
+            self.cont_capacity = cap
+            self.cont_num_layers = num_layers
+            self.use_contiguous = True
+            return True
         self.use_contiguous = False
         return False
 
+    def _release_window(self) -> None:
+        if self._window_pool is not None:
+            self._window_pool.release_window([s for v in self._window.values() for s in v])
+        self._window = {}
+        self._window_pool = None
+
     def prefill_contiguous(self, layer_id: int, K: torch.Tensor, V: torch.Tensor):
-        n = K.shape[2]
-        self.cont_K[layer_id][:, :, :n, :].copy_(K)
-        self.cont_V[layer_id][:, :, :n, :].copy_(V)
+        """Called after append_prefill (kv_offload.py:197-204): the pages already
+        hold the chunk, so only the counters move (layer 0 sets them, as the
+        reference does)."""
         if layer_id == 0:
-            self.cont_prefill_len = n
-            self.cont_seq_len = n
+            self.cont_prefill_len = K.shape[2]
+            self.cont_seq_len = K.shape[2]
+
+    def _window_row(self, layer_id: int) -> int:
+        """Pool row of the decode token being written (window position
+        cont_seq_len - cont_prefill_len)."""
+        P = self.allocator.page_size
+        i = self.cont_seq_len - self.cont_prefill_len
+        return self._window[layer_id][i // P] * P + i % P
+
+    def _window_pages(self, layer_id: int, n: int):
+        """(slots, used) of the first n window tokens."""
+        P = self.allocator.page_size
+        k = -(-n // P)
+        used = np.full(k, P, np.int32)
+        if k:
+            used[-1] = n - (k - 1) * P
+        return np.asarray(self._window[layer_id][:k], np.int32), used
 
     def write_decode_contiguous(self, layer_id: int, K_new: torch.Tensor, V_new: torch.Tensor):
-        idx = self.cont_seq_len
-        self.cont_K[layer_id][:, :, idx:idx + 1, :].copy_(K_new)
-        self.cont_V[layer_id][:, :, idx:idx + 1, :].copy_(V_new)
+        """Writes one decode token [1, H, 1, D] at the next window position."""
+        P = self.allocator.page_size
+        row = self._window_row(layer_id)
+        pool = self._window_pool
+        if pool.is_host:
+            pool.storage[row // P, 0, :, row % P].copy_(K_new[0, :, 0])
+            pool.storage[row // P, 1, :, row % P].copy_(V_new[0, :, 0])
+            return
+        rows = torch.tensor([row], dtype=torch.int64).pin_memory().to(pool.device,
+                                                                     non_blocking=True)
+        _capi.kv_append(k=K_new[:, :, 0, :].to(pool.dtype), v=V_new[:, :, 0, :].to(pool.dtype),
+                        pool=pool.storage, slot_rows=rows, page_size=P)
+
+    def _window_dense(self, layer_id: int, n: int) -> tuple:
+        """The first n window tokens as dense K, V [1, H, n, D] (a copy)."""
+        slots, _ = self._window_pages(layer_id, n)
+        st = self._window_pool.storage
+        idx = torch.as_tensor(slots.astype(np.int64), device=st.device)
+        H, P, D = st.shape[2], st.shape[3], st.shape[4]
+        blk = st.index_select(0, idx)                       # [k, 2, H, P, D]
+        kv = blk.permute(1, 2, 0, 3, 4).reshape(2, H, -1, D)[:, :, :n]
+        return kv[0].unsqueeze(0), kv[1].unsqueeze(0)
+
+    def _layer_dense(self, layer_id: int, n_window: int) -> tuple:
+        """Every cached token of the layer (pages, then window) as dense
+        K, V [1, H, T, D] (a copy)."""
+        ks, vs = [], []
+        for p in self.iterate_layer_pages(layer_id):
+            if p.used_tokens > 0 and p.state != "DEAD":
+                ks.append(p.k_tensor[:, :, :p.used_tokens])
+                vs.append(p.v_tensor[:, :, :p.used_tokens])
+        if n_window > 0:
+            k, v = self._window_dense(layer_id, n_window)
+            ks.append(k.to(ks[0].device) if ks else k)
+            vs.append(v.to(vs[0].device) if vs else v)
+        if not ks:
+            a = self.allocator
+            z = torch.zeros(1, a.num_kv_heads, 0, a.head_dim, dtype=a.dtype)
+            return z, z.clone()
+        dev = ks[-1].device
+        return torch.cat([k.to(dev) for k in ks], dim=2), torch.cat([v.to(dev) for v in vs], dim=2)
 
     def get_kv_contiguous(self, layer_id: int):
-        n = self.cont_seq_len + 1
-        return self.cont_K[layer_id][:, :, :n, :], self.cont_V[layer_id][:, :, :n, :]
+        """K, V [1, H, T, D] of the layer through the token just written (a
+        dense copy; the decode path itself reads pages and window in place)."""
+        return self._layer_dense(layer_id, self.cont_seq_len - self.cont_prefill_len + 1)
 
     def advance_contiguous(self):
+        """Commits the current decode token (after the last layer)."""
         self.cont_seq_len += 1
 
     def migrate_contiguous_to_pages(self):
-        if not self.cont_K:
+        """Appends the window's decode tokens to every layer's pages, as the
+        reference's bulk append_prefill of them does, then drops the window."""
+        if not self._window:
             return
         s, e = self.cont_prefill_len, self.cont_seq_len
         if e > s:
             for lid in range(self.cont_num_layers):
-                self.append_prefill(lid, self.cont_K[lid][:, :, s:e, :],
-                                    self.cont_V[lid][:, :, s:e, :])
+                k, v = self._window_dense(lid, e - s)
+                self.append_prefill(lid, k, v)
         self.drop_contiguous()
 
     def drop_contiguous(self):
-        self.cont_K.clear()
-        self.cont_V.clear()
+        """Returns the window's slots to the pool; decode continues on pages."""
+        self._release_window()
         self.use_contiguous = False
 
     def reset_contiguous(self):
-        if self.cont_K:
+        """Re-arms the window for the next generate() when it is still reserved."""
+        if self._window:
             self.use_contiguous = True
             self.cont_seq_len = 0
             self.cont_prefill_len = 0
+
+    @property
+    def cont_K(self) -> dict:
+        """The reference's per-layer buffers, [1, H, capacity, D]: assembled on
+        access from pages and window (zeros past the cached tokens)."""
+        return self._window_buffers(0)
+
+    @property
+    def cont_V(self) -> dict:
+        return self._window_buffers(1)
+
+    def _window_buffers(self, kv: int) -> dict:
+        out = {}
+        for lid in self._window:
+            n_win = max(0, self.cont_seq_len - self.cont_prefill_len)
+            dense = self._layer_dense(lid, n_win)[kv]
+            a = self.allocator
+            buf = torch.zeros(1, a.num_kv_heads, self.cont_capacity, a.head_dim, dtype=a.dtype,
+                              device=self._window_pool.device)
+            n = min(dense.shape[2], self.cont_capacity)
+            buf[:, :, :n] = dense[:, :, :n].to(buf.device)
+            out[lid] = buf
+        return out
 
     def layers_keys(self):
         return sorted(self.layers.keys())

@@ -66,10 +66,27 @@ class KVOffloadConfig:
 
 
 # ── decode step ─────────────────────────────────────────────────────────────────
+def _in_window(kvcms) -> bool:
+    """Path 1 of kv_offload.py:115-142: while the all-GPU window has room the
+    decode token goes to the window; at capacity every item's window is
+    migrated to pages and the step continues on pages."""
+    k0 = kvcms[0]
+    if not k0.use_contiguous:
+        return False
+    if k0.cont_seq_len < k0.cont_capacity:
+        return True
+    for kvcm in kvcms:
+        kvcm.migrate_contiguous_to_pages()
+    return False
+
+
 def _reserve_rows(kvcms, layer_idx: int, device) -> np.ndarray:
     """Reference-order bookkeeping of one decode append per item
     (append_decode + residency, kv_offload.py:146-148), with the eviction
-    copies deferred until the new rows are written.  Returns pool rows."""
+    copies deferred until the new rows are written.  Returns pool rows (the
+    window rows during the all-GPU window phase)."""
+    if _in_window(kvcms):
+        return np.array([kvcm._window_row(layer_idx) for kvcm in kvcms], np.int64)
     rows = np.empty(len(kvcms), np.int64)
     P = kvcms[0].allocator.page_size
     for kvcm in kvcms:
@@ -96,11 +113,25 @@ def _attend_layer(kvcms, layer_idx: int, q3: torch.Tensor, scale: float,
     dev = q3.device
     pool = _device_pool(kvcms, dev)
     t = _layer_tables(kvcms, layer_idx, pool)
+    if kvcms[0].use_contiguous:
+        if t is None:
+            raise RuntimeError("all-GPU window over pages edited by hand")
+        t = _with_window(kvcms, layer_idx, t, pool)
+        out = _attend_tables(kvcms, layer_idx, q3, pool, t, scale, attention_mask, softcap)
+        if layer_idx == kvcms[0].cont_num_layers - 1:
+            for kvcm in kvcms:
+                kvcm.advance_contiguous()
+        return out
     if t is None:  # pages edited by hand: page-object path
         lists = [[p for p in k.iterate_layer_pages(layer_idx)
                   if p.used_tokens > 0 and p.state != "DEAD"] for k in kvcms]
         T = max(sum(p.used_tokens for p in l) for l in lists)
         return _attend_lists(q3, lists, scale, _mask_2d(attention_mask, T, dev), softcap)
+    return _attend_tables(kvcms, layer_idx, q3, pool, t, scale, attention_mask, softcap)
+
+
+def _attend_tables(kvcms, layer_idx, q3, pool, t, scale, attention_mask, softcap):
+    dev = q3.device
     T = int(t.used.sum(axis=1).max()) if t.used.size else 0
     mask2d = _mask_2d(attention_mask, T, dev)
     key = (id(kvcms[0]), layer_idx)
@@ -108,6 +139,33 @@ def _attend_layer(kvcms, layer_idx: int, q3: torch.Tensor, scale: float,
                          parity=layer_idx & 1)
     _prefetch_layer(kvcms, layer_idx + 1, pool, dev)
     return out
+
+
+def _with_window(kvcms, layer_idx: int, t, pool):
+    """Appends every item's window pages (decode tokens through the current
+    one) to its page list; ragged when a list's last page before the window is
+    partial (the prefill's tail)."""
+    if any(k._window_pool is not pool for k in kvcms):
+        raise RuntimeError("all-GPU window on another device than the query")
+    n_win = kvcms[0].cont_seq_len - kvcms[0].cont_prefill_len + 1
+    extra = -(-n_win // kvcms[0].allocator.page_size)
+    nseq, maxp = t.slots.shape
+    slots = np.zeros((nseq, maxp + extra), np.int32)
+    used = np.zeros_like(slots)
+    nump = t.nump.copy()
+    ragged = t.ragged
+    P = kvcms[0].allocator.page_size
+    for b, kvcm in enumerate(kvcms):
+        n = int(t.nump[b])
+        slots[b, :n] = t.slots[b, :n]
+        used[b, :n] = t.used[b, :n]
+        if n and used[b, n - 1] != P:
+            ragged = True
+        s_b, u_b = kvcm._window_pages(layer_idx, n_win)
+        slots[b, n:n + extra] = s_b
+        used[b, n:n + extra] = u_b
+        nump[b] = n + extra
+    return type(t)(slots, used, nump, ragged, t.cold, t.cold_pos)
 
 
 def _prefetch_layer(kvcms, layer_idx: int, pool, dev) -> None:
@@ -200,6 +258,8 @@ def _append_prefill_batched(kvcms, k, v, layer_idx: int) -> list:
     for i in range(k.shape[0]):
         past_lengths.append(_cached_tokens(kvcms[i], layer_idx))
         kvcms[i].append_prefill(layer_idx, k[i:i + 1], v[i:i + 1])
+        if getattr(kvcms[i], "use_contiguous", False):
+            kvcms[i].prefill_contiguous(layer_idx, k[i:i + 1], v[i:i + 1])
     return past_lengths
 
 
@@ -467,8 +527,9 @@ class KVOffloadManager:
     split across items (kv_offload.py:683-689).
 
     Only modules whose parameters live on a CUDA device are patched; CPU-stage
-    layers keep the model's own forward.  The contiguous (all-GPU) buffers of
-    the reference are not built: the paged kernel serves that case directly.
+    layers keep the model's own forward.  config.cont_capacity > 0 on a CUDA
+    model reserves the all-GPU decode window of every item
+    (KVCacheManager.build_contiguous; kv_offload.py:697-713): all or none.
     """
 
     _ARCHS = ("qwen3", "qwen2", "gemma2", "ministral", "olmo2", "mistral", "llama")
@@ -489,6 +550,18 @@ class KVOffloadManager:
         self._patched_instance_forwards: dict = {}
         self._apply_patches(model)
         self.patch_module_roots(model)
+        if config.cont_capacity > 0:
+            device = next(model.parameters()).device
+            if device.type == "cuda":
+                built = [kvcm.build_contiguous(num_layers=config.num_layers,
+                                               num_kv_heads=config.num_kv_heads,
+                                               head_dim=config.head_dim,
+                                               capacity=config.cont_capacity, device=device,
+                                               dtype=config.dtype)
+                         for kvcm in self.kvcms]
+                if not all(built):
+                    for kvcm in self.kvcms:
+                        kvcm.drop_contiguous()
 
     def reset(self):
         """Clears every paged cache (kv_offload.py:717-721)."""

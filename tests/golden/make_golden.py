@@ -254,31 +254,46 @@ def _scenarios():
     return sc
 
 
-def make_placement(ref, out_path: str):
-    import helm.runtime.kv_allocator as ka
-    import helm.runtime.kv_cache as kc
+class _FakeCudaTensor(torch.Tensor):
+    """A CPU tensor whose .device reads 'cuda:0' (the policy's only GPU test)."""
 
-    class FakeCudaTensor(torch.Tensor):
-        """A CPU tensor whose .device reads 'cuda:0' (the policy's only GPU test)."""
+    @property
+    def device(self):
+        return torch.device("cuda:0")
 
-        @property
-        def device(self):
-            return torch.device("cuda:0")
 
-    real_empty = torch.empty
+def _fake_cuda_torch():
+    """A stand-in for the torch module inside the reference's kv modules:
+    tensors requested on a CUDA device are made on the CPU and labelled
+    'cuda', so the GPU-tier policy runs without a GPU."""
+    real_empty, real_zeros = torch.empty, torch.zeros
+
+    def on_fake_cuda(fn, a, kw):
+        dev = kw.get("device")
+        if dev is not None and torch.device(dev).type == "cuda":
+            kw["device"] = "cpu"
+            return fn(*a, **kw).as_subclass(_FakeCudaTensor)
+        return fn(*a, **kw)
 
     class TorchShim:
         def __getattr__(self, n):
             return getattr(torch, n)
 
         def empty(self, *a, **kw):
-            dev = kw.get("device")
-            if dev is not None and torch.device(dev).type == "cuda":
-                kw["device"] = "cpu"
-                return real_empty(*a, **kw).as_subclass(FakeCudaTensor)
-            return real_empty(*a, **kw)
+            return on_fake_cuda(real_empty, a, kw)
 
-    ka.torch = TorchShim()
+        def zeros(self, *a, **kw):
+            return on_fake_cuda(real_zeros, a, kw)
+
+    return TorchShim()
+
+
+def make_placement(ref, out_path: str):
+    import helm.runtime.kv_allocator as ka
+    import helm.runtime.kv_cache as kc
+
+    FakeCudaTensor = _FakeCudaTensor
+    ka.torch = _fake_cuda_torch()
     results = []
     for sc in _scenarios():
         dtype = {4: torch.float32, 2: torch.bfloat16}[sc["elem_bytes"]]
@@ -463,19 +478,79 @@ def make_prefill(ref, out_path: str):
     np.savez_compressed(out_path, **arrays)
 
 
+# ---------------------------------------------------------------- contiguous --
+def make_contiguous(ref, out_path: str):
+    """The all-GPU contiguous path of _decode_batched (kv_offload.py:115-142)
+    as HELM's inference front end enables it (cont_capacity set,
+    inference.py:729-731): one prefill of 37 tokens, then decode steps; the
+    first 27 go to the contiguous buffers, at cont_capacity = 64 the decode
+    tokens migrate to pages (kv_cache.py:317-335) and the rest run on pages.
+    GPU-tier placement via 'cuda'-labelled CPU tensors, as in placement.json.
+    Stores inputs, every step's attention output, the counters after every
+    step and the final page placement."""
+    import helm.runtime.kv_allocator as ka
+    import helm.runtime.kv_cache as kc
+    import helm.runtime.kv_offload as ko
+    shim = _fake_cuda_torch()
+    ka.torch = shim
+    kc.torch = shim
+    L, B, Hq, Hkv, D, P, S, CAP, STEPS = 2, 2, 4, 2, 64, 16, 37, 64, 35
+    dtype = torch.bfloat16
+    gen = torch.Generator().manual_seed(2024)
+    pre_k = torch.randn(L, B, Hkv, S, D, generator=gen).to(dtype)
+    pre_v = torch.randn(L, B, Hkv, S, D, generator=gen).to(dtype)
+    qs = torch.randn(STEPS, L, B, Hq, 1, D, generator=gen).to(dtype)
+    ks = torch.randn(STEPS, L, B, Hkv, 1, D, generator=gen).to(dtype)
+    vs = torch.randn(STEPS, L, B, Hkv, 1, D, generator=gen).to(dtype)
+    alloc = ka.KVAllocator(L, Hkv, D, page_size=P, dtype=dtype)
+    kc.reset_paging_stats()
+    mgrs = [kc.KVCacheManager(alloc, gpu_high_watermark_bytes=10 ** 12) for _ in range(B)]
+    for m in mgrs:
+        assert m.build_contiguous(num_layers=L, num_kv_heads=Hkv, head_dim=D, capacity=CAP,
+                                  device=torch.device("cuda:0"), dtype=dtype)
+    fake = (lambda t: t.clone().as_subclass(_FakeCudaTensor))
+    for lid in range(L):
+        ko._append_prefill_batched(mgrs, fake(pre_k[lid]), fake(pre_v[lid]), lid)
+    outs, counters = [], []
+    scale = D ** -0.5
+    for st in range(STEPS):
+        for lid in range(L):
+            o = ko._decode_batched(mgrs, fake(qs[st, lid]), fake(ks[st, lid]),
+                                   fake(vs[st, lid]), lid, scale)
+            outs.append(torch.Tensor(o).as_subclass(torch.Tensor)[:, :, 0].clone())
+        counters.append([int(mgrs[0].use_contiguous), mgrs[0].cont_seq_len,
+                         mgrs[0].cont_prefill_len])
+    placement = []
+    for b, m in enumerate(mgrs):
+        for lid in sorted(m.layers):
+            for p in m.layers[lid].pages:
+                placement.append([b, lid, p.page_id, p.start_token, p.used_tokens,
+                                  p.capacity_tokens, 1 if p.state == "GPU" else 0])
+    np.savez_compressed(
+        out_path, pre_k=_bits(pre_k), pre_v=_bits(pre_v), q=_bits(qs), k=_bits(ks), v=_bits(vs),
+        out=_bits(torch.stack(outs).view(STEPS, L, B, Hq, D)),
+        counters=np.array(counters, np.int64), placement=np.array(placement, np.int64),
+        meta=np.array([L, B, Hq, Hkv, D, P, S, CAP, STEPS], np.int64))
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("HELM_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["attention", "placement", "norm_rope", "prefill"],
+    ap.add_argument("--ref", default=os.environ.get("HELM_REFERENCE"),
+                    help="HELM checkout to run (default: $HELM_REFERENCE)")
+    ap.add_argument("--only", choices=["attention", "placement", "norm_rope", "prefill",
+                                       "contiguous"],
                     default=None)
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the HELM checkout with --ref or HELM_REFERENCE")
     sys.path.insert(0, args.ref)
     import helm  # noqa: F401  (fails loudly when the reference is absent)
     torch.manual_seed(0)
     makers = {"attention": (make_attention, "attention.npz"),
               "placement": (make_placement, "placement.json"),
               "norm_rope": (make_norm_rope, "norm_rope.npz"),
-              "prefill": (make_prefill, "prefill.npz")}
+              "prefill": (make_prefill, "prefill.npz"),
+              "contiguous": (make_contiguous, "contiguous.npz")}
     for key, (fn, fname) in makers.items():
         if args.only is None or args.only == key:
             fn(args.ref, os.path.join(HERE, fname))

@@ -7,11 +7,11 @@ The reference's tests import `helm.runtime.kv_allocator` and
 `helm.runtime.kv_cache`; a throw-away package named `helm` in a temporary
 directory re-exports helm_b200.runtime's modules under those names, the two
 test files are copied next to it, and pytest runs them there (nothing is
-written into the reference checkout).  The outcome is stored in
-tests/golden/reference_unit_tests.txt.  Tests that need a GPU skip on a
-machine without one.  The reference's attention tests are not run: they
-compute attention for queries on the CPU, which helm_b200 leaves to HELM's own
-code.
+written into the reference checkout or this repository).  Tests that need a
+GPU skip on a machine without one; their restatements run on the GPU in
+tests/test_reference_cases_gpu.py.  The reference's attention tests are not
+run: they compute attention for queries on the CPU, which helm_b200 leaves to
+HELM's own code.
 """
 from __future__ import annotations
 
@@ -32,8 +32,11 @@ globals().update({{k: getattr(_m, k) for k in dir(_m) if not k.startswith("__")}
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("HELM_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("HELM_REFERENCE"),
+                    help="HELM checkout whose tests to run (default: $HELM_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give the HELM checkout with --ref or HELM_REFERENCE")
     src = os.path.join(args.ref, "tests", "unit", "runtime")
     with tempfile.TemporaryDirectory() as tmp:
         pkg = os.path.join(tmp, "helm", "runtime")
@@ -50,13 +53,7 @@ def main():
         res = subprocess.run([sys.executable, "-m", "pytest", "-q", "-rs", "-p",
                               "no:cacheprovider", *FILES], cwd=tmp, env=env,
                              capture_output=True, text=True)
-    report = res.stdout.strip().splitlines()
-    out = os.path.join(HERE, "reference_unit_tests.txt")
-    with open(out, "w") as f:
-        f.write("HELM's tests/unit/runtime/{" + ",".join(FILES) + "} run against "
-                "helm_b200.runtime (tests/golden/run_reference_tests.py)\n\n")
-        f.write("\n".join(report[-20:]) + "\n")
-    print("\n".join(report[-5:]))
+    print("\n".join(res.stdout.strip().splitlines()[-20:]))
     return res.returncode
 
 

@@ -22,6 +22,10 @@ def test_reference_arm_json_line():
     assert d["impl"] == "reference" and d["n_gpus"] == 1 and d["steps"] == 1
     assert d["value"] > 0 and d["higher_is_better"] is True
     assert d["config"]["workload"].startswith("config2")
+    # both arms print the same config dict (the GPU arm builds it with the same function)
+    sys.path.insert(0, REPO)
+    import bench
+    assert d["config"] == json.loads(json.dumps(bench._config()))
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0,

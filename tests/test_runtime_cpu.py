@@ -192,11 +192,53 @@ def test_evict_without_gpu_pages_is_noop(cache):
 
 
 def test_contiguous_capacities():
-    mgr = KVCacheManager(_alloc(), gpu_high_watermark_bytes=0)
-    for cap in (64, 640, 2048):
+    """reference test_kv_cache.py:501-513: small capacities are honoured; the
+    window is a reservation of ceil(capacity / page_size) slots per layer."""
+    alloc = _alloc()
+    mgr = KVCacheManager(alloc, gpu_high_watermark_bytes=0)
+    pool = alloc.pool_for(CPU)
+    for cap in (64, 640, 768, 2048):
         assert mgr.build_contiguous(2, 2, 8, cap, CPU, torch.float32)
         assert mgr.use_contiguous and mgr.cont_capacity == cap
         assert mgr.cont_K[0].shape == (1, 2, cap, 8)
+        assert len(pool.window) == 2 * -(-cap // alloc.page_size)
+    mgr.drop_contiguous()
+    assert not pool.window and not mgr.use_contiguous
+
+
+def test_contiguous_window_halves_when_the_pool_cannot_grow(monkeypatch):
+    """build_contiguous retries with half the capacity down to
+    min(capacity, 1024) tokens (kv_cache.py:272-300)."""
+    alloc = _alloc()
+    mgr = KVCacheManager(alloc, gpu_high_watermark_bytes=0)
+    pool = alloc.pool_for(CPU)
+    real = pool.reserve_window
+
+    def limited(n):           # room for 1024 tokens per layer at most
+        if n > 2 * 1024 // alloc.page_size:
+            raise RuntimeError("out of memory")
+        return real(n)
+    monkeypatch.setattr(pool, "reserve_window", limited)
+    assert mgr.build_contiguous(2, 2, 8, 2048, CPU, torch.float32)
+    assert mgr.cont_capacity == 1024 and mgr.use_contiguous
+    # 3000 -> 1500 -> 750 < the floor of 1024: gives up
+    assert not mgr.build_contiguous(2, 2, 8, 3000, CPU, torch.float32)
+    assert not mgr.use_contiguous and not pool.window
+
+
+def test_contiguous_window_slots_are_never_given_to_pages():
+    alloc = _alloc()
+    mgr = KVCacheManager(alloc, gpu_high_watermark_bytes=10 ** 9)
+    assert mgr.build_contiguous(2, 2, 8, 40, CPU, torch.float32)
+    window = set(alloc.pool_for(CPU).window)
+    k = torch.randn(1, 2, 50, 8)
+    mgr.append_prefill(0, k, k)
+    mgr.append_prefill(1, k, k)
+    slots = {p.slot for L in mgr.layers.values() for p in L.pages}
+    assert not slots & window
+    mgr.drop_contiguous()
+    mgr.append_prefill(0, k, k)   # released slots are reused
+    assert {p.slot for p in mgr.layers[0].pages} & window
 
 
 # ── stats (reference test_kv_cache.py:321-362) ─────────────────────────────────
