@@ -856,6 +856,27 @@ def _h2d_gbs(dev: torch.device, nbytes: int = 1 << 30) -> float:
     return best
 
 
+def _time_cold_copies(gd, dev: torch.device, reps: int = 3) -> float:
+    """Milliseconds the copy engine needs for one step's cold-page copies
+    alone (the same per-layer copy lists the captured step issues, on an idle
+    GPU, best of `reps`)."""
+    from helm_b200 import _capi
+    ctx = gd.ctx
+    s = torch.cuda.Stream(dev)
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(s)
+        for plan in ctx.cold_plan:
+            for host_pool, srcs, dsts in plan:
+                _capi.copy_pages(ctx.pool.storage, host_pool.storage, dsts, srcs, dev, stream=s)
+        e1.record(s)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return best
+
+
 def run_model(args, rank: int, world: int, dev: torch.device):
     """Decode tok/s of a whole model: random-init
     weights, random prompt, greedy decode through KVOffloadManager + GraphDecoder
@@ -900,6 +921,23 @@ def run_model(args, rank: int, world: int, dev: torch.device):
         h2d_step = gd.h2d_bytes / K
         plan_ms = gd.plan_seconds * 1e3 / K
         captures = gd.captures
+        prefetch = None
+        if w["cold"] > 0:
+            # the two bounds of a step with cold pages, measured: the step's copies alone
+            # on the copy engine, and the same decode with every page resident in HBM
+            copy_ms = _time_cold_copies(gd, dev)
+            mgr.restore()
+            mgr = KVOffloadManager(model, KVOffloadConfig.from_model(
+                model, page_size=w["page"], gpu_watermark_bytes=1 << 50))
+            gd_hot = GraphDecoder(model, mgr, max_len=S + K + 1, fused=args.stage == "fused")
+            gd_hot.generate(prompt.to(dev, non_blocking=True), 4)
+            gd_hot.generate(prompt.to(dev, non_blocking=True), K + 1)
+            hot_ms = gd_hot.decode_ms() / K
+            prefetch = {"copy_alone_ms_per_step": copy_ms, "all_resident_ms_per_step": hot_ms,
+                        "h2d_gbs_copy_alone": h2d_step / (copy_ms / 1e3) / 1e9,
+                        "overlap": ms / max(copy_ms, hot_ms),
+                        "note": "overlap = step time / max(copies alone, all-resident step); "
+                                "1.0 = the slower of the two fully hides the other"}
     finally:
         mgr.restore()
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -952,6 +990,7 @@ def run_model(args, rank: int, world: int, dev: torch.device):
                     "d2h_bytes_per_step": toks_host.numel() * 8 / (K + 1),
                     "note": "one generate() call from a pinned host prompt to host tokens, "
                             "prefill and graph captures included"},
+            "prefetch": prefetch,
             "host_plan_ms_per_step": plan_ms, "graph_captures": captures,
             "paging": stats,
             # this library's kernels per step: per layer append + attention (+ merge) and,

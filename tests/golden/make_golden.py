@@ -22,6 +22,13 @@ inputs plus the reference's outputs:
                   pages) under HELM's chunk-prefill mask
                   (pipeline_runtime.py:96-112), as _stream_prefill_batched
                   calls it (kv_offload.py:206-227)
+  contiguous.npz  _decode_batched on the all-GPU contiguous path and its
+                  migration to pages (kv_offload.py:115-142)
+  config1_pipeline.npz
+                  BASELINE configs[0] (Qwen3-0.6B architecture, seed-0
+                  weights, 512-token prompt, 64 greedy steps) through the
+                  reference's compile -> StageRuntimeExecutor ->
+                  KVOffloadManager -> PipelineRuntime path, fp32 on the CPU
 
 The fixtures are committed; this script is only needed to regenerate them.
 """
@@ -533,12 +540,89 @@ def make_contiguous(ref, out_path: str):
         meta=np.array([L, B, Hq, Hkv, D, P, S, CAP, STEPS], np.int64))
 
 
+# ------------------------------------------------------------------- config 1 --
+def make_config1(ref, out_path: str):
+    """BASELINE configs[0] through the reference's own pipeline, as its
+    execute_stagewise mode runs it (helm/_pipeline.py:530-573): the
+    Qwen3-0.6B architecture with seed-0 N(0, 0.02) weights (helm_b200.synthetic,
+    rounded to bf16 so that the GPU run loads the same model), in fp32 on the
+    CPU, a 512-token random prompt, FX capture -> compile_graph with a manual
+    all-CPU plan -> DecodeTracer -> StageRuntimeExecutor -> KVOffloadManager
+    (default config: 64-token pages) -> PipelineRuntime.generate, 64 greedy
+    steps.  Stores the tokens, the full logits of the first step and the
+    top-32 logits of every step."""
+    import tempfile
+    sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+    import helm.kernels as hk
+    from helm._pipeline import capture_decode_fx_graph, capture_fx_graph
+    from helm.compiler.compiler import HelmCompileOptions, compile_graph
+    from helm.compiler.importers.decode_tracer import DecodeTracer
+    from helm.runtime.executor import StageRuntimeExecutor
+    from helm.runtime.kv_offload import KVOffloadConfig, KVOffloadManager
+    from helm.runtime.pipeline_runtime import PipelineRuntime
+    from helm_b200.synthetic import build_model, make_config
+    hk._load_error = "not built: fp32 weights take torch's linear"   # no JIT build
+    torch.set_num_threads(os.cpu_count() or 1)
+    S, STEPS = 512, 64
+    cfg = make_config("qwen3-0.6b")
+    model = build_model(cfg, seed=0, std=0.02, dtype=torch.bfloat16, device="cpu").float()
+    ids = torch.randint(0, cfg.vocab_size, (1, S), generator=torch.Generator().manual_seed(0))
+    mask_dtype = torch.float16
+    causal = torch.triu(torch.full((S, S), torch.finfo(mask_dtype).min, dtype=mask_dtype),
+                        diagonal=1)[None, None]
+    dummy = (ids, causal, torch.arange(S).unsqueeze(0), torch.arange(S))
+    L = cfg.num_hidden_layers
+
+    def options(kind):
+        return HelmCompileOptions(
+            mode="both", objective="decode_latency", plan_mode="manual",
+            cpu_layers=f"0:{L - 1}", gpu_layers=None, lower_stages=True, graph_kind=kind,
+            model_name="qwen3-0.6b-random", kv_offload=True,
+            workload={"batch_size": 1, "prefill_seq_len": S, "decode_context_len": S,
+                      "decode_tokens": STEPS, "dtype_size": 2})
+    with tempfile.TemporaryDirectory() as run_dir:
+        gm = capture_fx_graph(model, dummy, run_dir, allow_fallback=True,
+                              trace_policy="explicit_leaf")
+        pre = compile_graph(gm=gm, example_inputs=dummy, model=model, tokenizer=None,
+                            options=options("prefill"), artifacts_dir=run_dir)
+        dd = DecodeTracer.build_dummy_inputs(device="cpu", batch_size=1, dtype=mask_dtype)
+        dgm = capture_decode_fx_graph(model, dd, run_dir)
+        dec = compile_graph(gm=dgm, example_inputs=dd, model=model, tokenizer=None,
+                            options=options("decode"), partition_plan_override=pre.partition_plan,
+                            artifacts_dir=os.path.join(run_dir, "decode"))
+        mgr = KVOffloadManager(model, KVOffloadConfig.from_model(model))
+        pexec, dexec = StageRuntimeExecutor(pre.stage_graphs), StageRuntimeExecutor(dec.stage_graphs)
+        mgr.patch_module_roots(*(st.module for st in pexec.stages),
+                               *(st.module for st in dexec.stages))
+        rt = PipelineRuntime(pexec, dexec, tokenizer=None, dtype=mask_dtype, kv_offload_mgr=mgr)
+        seen = []
+        select, step = rt._select_next_token_logits, rt.decode_step
+
+        def select_rec(logits, lengths):
+            out = select(logits, lengths)
+            seen.append(out[0].float().clone())
+            return out
+
+        def step_rec(*a, **kw):
+            out = step(*a, **kw)
+            seen.append(out[0, -1].float().clone())
+            return out
+        rt._select_next_token_logits, rt.decode_step = select_rec, step_rec
+        toks = rt.generate(ids, STEPS)
+    logits = torch.stack(seen[:STEPS])                       # [64, vocab]
+    top = torch.topk(logits, 32, dim=-1)
+    assert torch.equal(top.indices[:, 0], toks[0]), "argmax of the recorded logits"
+    np.savez_compressed(out_path, prompt=ids[0].numpy(), tokens=toks[0].numpy(),
+                        logits0=logits[0].numpy(), top_ids=top.indices.numpy(),
+                        top_vals=top.values.numpy())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("HELM_REFERENCE"),
                     help="HELM checkout to run (default: $HELM_REFERENCE)")
     ap.add_argument("--only", choices=["attention", "placement", "norm_rope", "prefill",
-                                       "contiguous"],
+                                       "contiguous", "config1"],
                     default=None)
     args = ap.parse_args()
     if not args.ref:
@@ -550,7 +634,8 @@ def main():
               "placement": (make_placement, "placement.json"),
               "norm_rope": (make_norm_rope, "norm_rope.npz"),
               "prefill": (make_prefill, "prefill.npz"),
-              "contiguous": (make_contiguous, "contiguous.npz")}
+              "contiguous": (make_contiguous, "contiguous.npz"),
+              "config1": (make_config1, "config1_pipeline.npz")}
     for key, (fn, fname) in makers.items():
         if args.only is None or args.only == key:
             fn(args.ref, os.path.join(HERE, fname))
