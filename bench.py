@@ -545,7 +545,10 @@ def _tp_decode(name: str, args, rank: int, world: int, dev: torch.device, steps:
         tp = SeqSplitDecodeModel(shard, batch=Bq, context_len=ctx,
                                  max_new=3 + W + K + e2e_steps + 16, page_size=16)
     else:
-        shard = synthetic_shard(arch, rank, world, w["dtype"], dev)
+        # --shard-of N on one GPU: rank 0's shard of an N-way split, run without the
+        # exchange (per-rank kernel shapes of N GPUs, for profiling on one GPU)
+        n_split = getattr(args, "shard_of", 0) or world
+        shard = synthetic_shard(arch, rank if n_split == world else 0, n_split, w["dtype"], dev)
         tp = TPDecodeModel(shard, batch=Bq, max_len=ctx + 3 + W + K + e2e_steps + 16,
                            page_size=16)
     try:
@@ -666,6 +669,9 @@ def _model_block(r: dict, world: int) -> dict:
 GEMV_SHAPES = {  # one Qwen3-14B layer at batch 1: (rows, input width, SwiGLU)
     "qkv": (7168, 5120, False), "o": (5120, 5120, False), "gateup": (17408, 5120, True),
     "down": (5120, 17408, False),
+    # the same layer's per-rank shapes under 8-way tensor parallelism
+    "qkv_tp8": (896, 5120, False), "o_tp8": (5120, 640, False),
+    "gateup_tp8": (2176, 5120, True), "down_tp8": (5120, 2176, False),
 }
 
 
@@ -676,17 +682,32 @@ def run_gemv(args, rank: int, world: int, dev: torch.device):
     them.  --gemv-shape restricts the run to one shape (eager calls only), the
     form used for an ncu capture."""
     from helm_b200 import _capi
-    shapes = [args.gemv_shape] if args.gemv_shape else list(GEMV_SHAPES)
+    if world > 1:
+        return _run_allreduce_gemv(args, rank, world, dev)
+    tp8 = args.gemv_set == "tp8"
+    shapes = [args.gemv_shape] if args.gemv_shape else \
+        [n for n in GEMV_SHAPES if n.endswith("_tp8") == tp8]
     per, tot_bytes, tot_us = {}, 0, 0.0
     for name in shapes:
         N, K, glu = GEMV_SHAPES[name]
         g = torch.Generator(device=dev).manual_seed(0)
-        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
-        w2 = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16) if glu else None
+        # distinct weight copies in turn, so that consecutive calls stream more than L2
+        nbytes = N * K * 2 * (2 if glu else 1)
+        copies = min(20, max(1, -(-(256 << 20) // nbytes)))
+        ws = [(torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+              for _ in range(copies)]
+        w2s = [(torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+               if glu else None for _ in range(copies)]
         x = torch.randn(1, K, device=dev, generator=g).to(torch.bfloat16)
-        nw = torch.ones(K, device=dev, dtype=torch.bfloat16) if name in ("qkv", "gateup") else None
+        nw = torch.ones(K, device=dev, dtype=torch.bfloat16) \
+            if name.startswith(("qkv", "gateup")) else None
         y = torch.empty(1, N, device=dev, dtype=torch.bfloat16)
-        fn = lambda: _capi.decode_gemv(x, w, out=y, norm_w=nw, w2=w2)  # noqa: E731
+        turn = [0]
+
+        def fn():
+            i = turn[0] % copies
+            turn[0] += 1
+            _capi.decode_gemv(x, ws[i], out=y, norm_w=nw, w2=w2s[i])
         for _ in range(max(args.warmup, 3)):
             fn()
         torch.cuda.synchronize(dev)
@@ -712,11 +733,10 @@ def run_gemv(args, rank: int, world: int, dev: torch.device):
         e1.record()
         torch.cuda.synchronize(dev)
         us = e0.elapsed_time(e1) * 1e3 / (20 * reps)
-        nbytes = N * K * 2 * (2 if glu else 1)
         per[name] = {"rows": N, "k": K, "swiglu": glu, "us": us, "gbs": nbytes / us / 1e3}
         tot_bytes += nbytes
         tot_us += us
-        del w, w2
+        del ws, w2s
     if rank != 0 or args.gemv_shape:
         return
     hbm, peak_src = _peaks()
@@ -726,12 +746,75 @@ def run_gemv(args, rank: int, world: int, dev: torch.device):
                       "warmup": args.warmup, "ms_per_step": tot_us / 1e3,
                       "higher_is_better": True, "scaling": "none", "vs_baseline": None,
                       "dtype": "bf16", "data": "synthetic",
-                      "config": {"workload": "gemv: the four projections of one Qwen3-14B layer",
+                      "config": {"workload": "gemv: the four projections of one Qwen3-14B layer"
+                                             + (" (per-rank shapes of 8-way tensor parallelism)"
+                                                if tp8 else "")
+                                             + "; consecutive calls use distinct weight copies "
+                                               "(more than L2 per 20 calls)",
                                  "shapes": per},
                       "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s",
                                    "frac": value / hbm, "traffic": None,
                                    "peak_source": peak_src},
                       "gpu_launches": 20 * max(1, args.steps // 20) * len(per)}), flush=True)
+
+
+def _run_allreduce_gemv(args, rank: int, world: int, dev: torch.device):
+    """The row-parallel projections of one Qwen3-14B layer under `world`-way
+    tensor parallelism (o_proj 5120 x 5120/N, down_proj 5120 x 17408/N, batch 1,
+    residual fused): helm_decode_gemv_allreduce against the same GEMV without
+    the exchange, each as CUDA graphs of 20 calls on rotating weight copies;
+    time = max over ranks.  The difference is what the all-reduce costs."""
+    from helm_b200 import _capi
+    from helm_b200.runtime.tp_decode import _PeerBuffers
+    shapes = {"o": (5120, 5120 // world), "down": (5120, 17408 // world)}
+    peers = _PeerBuffers(_capi.decode_gemv_allreduce_bytes(5120, 1, world), dev, None, rank,
+                         world)
+    res = {}
+    try:
+        for name, (N, K) in shapes.items():
+            g = torch.Generator(device=dev).manual_seed(rank)
+            copies = min(20, max(1, -(-(256 << 20) // (N * K * 2))))
+            ws = [(torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+                  for _ in range(copies)]
+            x = torch.randn(1, K, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.zeros(1, N, device=dev, dtype=torch.bfloat16)
+            for kind in ("plain", "allreduce"):
+                def call(i, kind=kind):
+                    if kind == "plain":
+                        _capi.decode_gemv(x, ws[i % copies], out=y, residual=y)
+                    else:
+                        _capi.decode_gemv_allreduce(peers.ptrs, rank, x, ws[i % copies], out=y,
+                                                    residual=y)
+                for i in range(4):
+                    call(i)
+                torch.cuda.synchronize(dev)
+                torch.distributed.barrier()
+                gr = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side), torch.cuda.graph(gr, stream=side):
+                    for i in range(20):
+                        call(i)
+                torch.cuda.current_stream(dev).wait_stream(side)
+                gr.replay()
+                reps = max(1, args.steps // 20)
+
+                def replays(n, gr=gr, reps=reps):
+                    for _ in range(reps):
+                        gr.replay()
+                ms, _, _ = _timed(replays, 1, world, dev, torch.cuda.current_stream(dev), False)
+                res.setdefault(name, {"rows": N, "k": K})[kind + "_us"] = ms * 1e3 / (20 * reps)
+                del gr
+            res[name]["allreduce_cost_us"] = res[name]["allreduce_us"] - res[name]["plain_us"]
+            del ws
+        status = _capi.device_status(dev)
+    finally:
+        peers.close()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+    if rank == 0:
+        print(json.dumps({"metric": "row-parallel GEMV with in-kernel all-reduce", "unit": "us",
+                          "n_gpus": world, "higher_is_better": False, "shapes": res}), flush=True)
 
 
 PREFILL = dict(Hq=40, Hkv=8, D=128, P=64, S=512)  # configs[3] (Qwen3-14B), one 512-token chunk
@@ -1012,6 +1095,9 @@ def main():
                     help="config2 (default, BASELINE configs[1]); the 128k-token attention of "
                          "configs[3] split across the GPUs (strong scaling); or whole-model "
                          "decode tok/s of configs[0] (config1) / configs[2] (config3)")
+    ap.add_argument("--gemv-set", choices=["full", "tp8"], default="full",
+                    help="gemv workload: the layer's shapes on one GPU, or one rank's under "
+                         "8-way tensor parallelism")
     ap.add_argument("--gemv-shape", choices=sorted(GEMV_SHAPES), default=None,
                     help="gemv workload: run one shape with eager calls (for an ncu capture)")
     ap.add_argument("--profile-step", action="store_true",
@@ -1026,6 +1112,9 @@ def main():
                          "(head), or the whole model on every rank with the K/V split by "
                          "token range and partial states merged over NVLink (sequence)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="config4/config5 on one GPU: run rank 0's shard of an N-way tensor-"
+                         "parallel split without the exchange (per-rank shapes, profiling)")
     ap.add_argument("--no-model-block", action="store_true",
                     help="default workload: skip the config-4 model-decode block")
     ap.add_argument("--seq-len", type=int, default=T,

@@ -573,9 +573,10 @@ def gemv_max_batch(k: int, elem: int = 2) -> int:
     every batch row plus the weight-stream ring must fit in shared memory."""
     for nb in (16, 8, 4, 2, 1):
         threads = 512 if nb == 1 else 256
-        ring = 128 if nb >= 8 else 256
+        ring = 128 if nb >= 8 or nb == 1 else 256
         stride = k if nb == 1 else k + 8
         static = 4 * (threads // 32) * 16 * nb * 2 + 1024
-        if (nb * stride * elem + 127) // 128 * 128 + threads * ring + static <= 224 * 1024:
+        nw = (k * elem + 127) // 128 * 128 if nb == 1 else 0   # prefetched norm weight
+        if (nb * stride * elem + 127) // 128 * 128 + nw + threads * ring + static <= 224 * 1024:
             return nb
     raise HelmError(f"input width {k} too large for decode_gemv")

@@ -35,10 +35,18 @@ template <int NB>
 struct GemvShape {
   static constexpr int kThreads = NB == 1 ? 512 : 256;
   static constexpr int kWarps = kThreads / 32;
-  // bytes of weight stream in flight per lane (cp.async ring): 128 KB per CTA
+  // bytes of weight stream in flight per lane (cp.async ring): 64 KB per CTA
   // for one batch row (512 threads), 64 KB for 2-4 rows, 32 KB where x of 8-16
   // rows takes the shared memory
-  static constexpr int kRingPerLane = NB >= 8 ? 128 : 256;
+  static constexpr int kRingPerLane = (NB >= 8 || NB == 1) ? 128 : 256;
+  // One batch row: two CTAs per SM (registers capped at 64 per thread), so the
+  // grid holds 128 KB in flight per SM as before, and the next launch of a
+  // decode step (a programmatic dependent) finds room on every SM while this
+  // one streams: its ring fill and norm-weight prefetch run under it.
+  static constexpr int kMinBlocks = NB == 1 ? 2 : 1;
+  static constexpr int kStageV = NB == 1 ? 4 : 8;  // x chunks in flight per thread
+  static constexpr int kCcItemGlu = 2;     // 16-byte chunks per lane per ring item
+  static constexpr int kCcItemPlain = 4;
 };
 
 template <int NB>
@@ -46,9 +54,21 @@ __host__ __device__ __forceinline__ int64_t gemv_x_stride(int64_t k) {
   return NB == 1 ? k : k + 8;  // rows of x in smem start 4 banks apart
 }
 
+// Dynamic shared memory: x of NB rows, [the norm weight (one batch row with
+// RMSNorm: prefetched before the dependency wait)], the weight-stream ring.
 template <typename T, int NB>
-size_t gemv_smem_bytes(int64_t k) {
-  return (static_cast<size_t>(NB) * gemv_x_stride<NB>(k) * sizeof(T) + 127) / 128 * 128 +
+__host__ __device__ __forceinline__ size_t gemv_x_bytes(int64_t k) {
+  return (static_cast<size_t>(NB) * gemv_x_stride<NB>(k) * sizeof(T) + 127) / 128 * 128;
+}
+
+template <typename T, int NB>
+__host__ __device__ __forceinline__ size_t gemv_nw_bytes(int64_t k, bool norm) {
+  return (NB == 1 && norm) ? (static_cast<size_t>(k) * sizeof(T) + 127) / 128 * 128 : 0;
+}
+
+template <typename T, int NB>
+size_t gemv_smem_bytes(int64_t k, bool norm) {
+  return gemv_x_bytes<T, NB>(k) + gemv_nw_bytes<T, NB>(k, norm) +
          static_cast<size_t>(GemvShape<NB>::kThreads) * GemvShape<NB>::kRingPerLane;
 }
 
@@ -218,6 +238,140 @@ __device__ __forceinline__ void emit_value(const GemvArgs& a, int64_t row, int b
     static_cast<T*>(a.y)[b * a.y_stride + row] = from_float<T>(v);
 }
 
+template <typename T>
+__device__ __forceinline__ float sumsq8(const uint4& v) {
+  const float2 a = unpack2<T>(v.x), b = unpack2<T>(v.y), c = unpack2<T>(v.z), d = unpack2<T>(v.w);
+  float s = a.x * a.x;
+  s = fmaf(a.y, a.y, s);
+  s = fmaf(b.x, b.x, s);
+  s = fmaf(b.y, b.y, s);
+  s = fmaf(c.x, c.x, s);
+  s = fmaf(c.y, c.y, s);
+  s = fmaf(d.x, d.x, s);
+  s = fmaf(d.y, d.y, s);
+  return s;
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// RMSNorm of 8 elements, rounding as HF's module does: xn = dtype(x * scale),
+// y = dtype(w * xn).
+template <typename T>
+__device__ __forceinline__ uint4 norm8(const uint4& x, const uint4& w, float sc) {
+  const uint32_t xi[4] = {x.x, x.y, x.z, x.w}, wi[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 xv = unpack2<T>(xi[i]), wv = unpack2<T>(wi[i]);
+    o[i] = pack2<T>(wv.x * round_to<T>(xv.x * sc), wv.y * round_to<T>(xv.y * sc));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Stages the NB rows of x into shared memory xs[NB][XS] (rows >= batch are
+// zero), RMSNorm'd when norm_w is given.  Rows move as 16-byte chunks with
+// kStageV loads in flight per thread, so staging costs about one memory round
+// trip per pass: the first pass copies the raw row to shared memory and sums
+// its squares, the second reads it back, normalises it with the (vector-
+// loaded) norm weight and overwrites it.  Unaligned inputs take an element
+// loop.
+template <typename T, int NB, int kThreads, int kStageV>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, T* xs, int64_t XS, float* s_red,
+                                        float* s_scale, const T* nw_smem = nullptr) {
+  const int64_t K = a.k;
+  const int64_t chunks = K / 8;
+  const T* x = static_cast<const T*>(a.x);
+  const T* nw = static_cast<const T*>(a.norm_w);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool vec = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(nw) |
+                     static_cast<uintptr_t>(a.x_stride * sizeof(T))) & 15u) == 0;
+  for (int b = 0; b < NB; ++b) {
+    T* row = xs + b * XS;
+    uint4* row4 = reinterpret_cast<uint4*>(row);
+    if (b >= a.batch) {
+      for (int64_t c = tid; c < chunks; c += kThreads) row4[c] = make_uint4(0u, 0u, 0u, 0u);
+      continue;
+    }
+    const T* xb = x + b * a.x_stride;
+    float ss = 0.f;
+    if (vec) {
+      const uint4* src = reinterpret_cast<const uint4*>(xb);
+      for (int64_t c0 = 0; c0 < chunks; c0 += static_cast<int64_t>(kStageV) * kThreads) {
+        uint4 v[kStageV];
+#pragma unroll
+        for (int u = 0; u < kStageV; ++u) {
+          const int64_t c = c0 + u * kThreads + tid;
+          if (c < chunks) v[u] = src[c];
+        }
+#pragma unroll
+        for (int u = 0; u < kStageV; ++u) {
+          const int64_t c = c0 + u * kThreads + tid;
+          if (c < chunks) {
+            row4[c] = v[u];
+            if (nw != nullptr) ss += sumsq8<T>(v[u]);
+          }
+        }
+      }
+    } else {
+      for (int64_t i = tid; i < K; i += kThreads) {
+        const T v = xb[i];
+        row[i] = v;
+        const float f = to_float<T>(v);
+        ss = fmaf(f, f, ss);
+      }
+    }
+    if (nw == nullptr) continue;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) s_red[warp] = ss;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < kThreads / 32; ++w) t += s_red[w];
+      *s_scale = rsqrtf(t / static_cast<float>(K) + a.eps);
+    }
+    __syncthreads();
+    const float sc = *s_scale;
+    if (nw_smem != nullptr) {   // the norm weight is in shared memory already
+      const uint4* wsrc = reinterpret_cast<const uint4*>(nw_smem);
+      for (int64_t c = tid; c < chunks; c += kThreads) row4[c] = norm8<T>(row4[c], wsrc[c], sc);
+    } else if (vec) {
+      const uint4* wsrc = reinterpret_cast<const uint4*>(nw);
+      for (int64_t c0 = 0; c0 < chunks; c0 += static_cast<int64_t>(kStageV) * kThreads) {
+        uint4 wv[kStageV];
+#pragma unroll
+        for (int u = 0; u < kStageV; ++u) {
+          const int64_t c = c0 + u * kThreads + tid;
+          if (c < chunks) wv[u] = wsrc[c];
+        }
+#pragma unroll
+        for (int u = 0; u < kStageV; ++u) {
+          const int64_t c = c0 + u * kThreads + tid;
+          if (c < chunks) row4[c] = norm8<T>(row4[c], wv[u], sc);
+        }
+      }
+    } else {
+      for (int64_t i = tid; i < K; i += kThreads) {
+        const float xn = round_to<T>(to_float<T>(row[i]) * sc);   // x.to(dtype)
+        row[i] = from_float<T>(to_float<T>(nw[i]) * xn);          // weight * x
+      }
+    }
+    __syncthreads();
+  }
+  __syncthreads();
+}
+
 __device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes)
                : "memory");
@@ -319,39 +473,7 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
   }
 
   // ---- stage x (rows >= batch are zero), RMSNorm'd when norm_w is given ----
-  for (int b = 0; b < NB; ++b) {
-    if (b >= a.batch) {
-      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = from_float<T>(0.f);
-      continue;
-    }
-    const T* xb = x + b * a.x_stride;
-    if (nw == nullptr) {
-      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = xb[i];
-      continue;
-    }
-    float ss = 0.f;
-    for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
-      const float v = to_float<T>(xb[i]);
-      ss = fmaf(v, v, ss);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) s_red[warp] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-      for (int w = 0; w < kGemvWarps; ++w) t += s_red[w];
-      s_scale = rsqrtf(t / static_cast<float>(K) + a.eps);
-    }
-    __syncthreads();
-    const float sc = s_scale;
-    for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
-      const float xn = round_to<T>(to_float<T>(xb[i]) * sc);        // x.to(dtype)
-      xs[b * XS + i] = from_float<T>(to_float<T>(nw[i]) * xn);     // weight * x
-    }
-    __syncthreads();
-  }
-  __syncthreads();
+  stage_x<T, NB, kGemvThreads, GemvShape<NB>::kStageV>(a, xs, XS, s_red, &s_scale);
 
   float acc[NT][4], acc2[NT][4];
 #pragma unroll
@@ -480,19 +602,25 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
 // work units than the 16-row blocks of the tensor-core form, which matters
 // when one row of x leaves the tensor cores idle anyway.
 template <typename T, int NB, bool AR, bool GLU>
-__global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(GemvShape<NB>::kThreads, GemvShape<NB>::kMinBlocks)
+    decode_gemv_cc_kernel(const GemvArgs a) {
   constexpr int kGemvThreads = GemvShape<NB>::kThreads;
   constexpr int kGemvWarps = GemvShape<NB>::kWarps;
   constexpr int kStreams = GLU ? 2 : 1;
-  constexpr int kU = GLU ? 2 : 4;  // 16-byte chunks per lane (and stream) per ring item
+  // 16-byte chunks per lane (and stream) per ring item
+  constexpr int kU = GLU ? GemvShape<NB>::kCcItemGlu : GemvShape<NB>::kCcItemPlain;
   constexpr int kDepth = GemvShape<NB>::kRingPerLane / (16 * kU * kStreams);
   static_assert(kDepth >= 2, "ring needs two items");
   extern __shared__ __align__(128) uint8_t gemv_smem[];
   const int64_t K = a.k;
   const int64_t XS = gemv_x_stride<NB>(K);
   T* xs = reinterpret_cast<T*>(gemv_smem);  // [NB][XS]
+  const bool nw_pre = NB == 1 && a.norm_w != nullptr &&
+                      (reinterpret_cast<uintptr_t>(a.norm_w) & 15u) == 0;
+  T* nws = reinterpret_cast<T*>(gemv_smem + gemv_x_bytes<T, NB>(K));  // [K] when nw_pre
   const uint32_t ring = smem_addr(gemv_smem) +
-                        static_cast<uint32_t>((NB * XS * sizeof(T) + 127) / 128 * 128);
+                        static_cast<uint32_t>(gemv_x_bytes<T, NB>(K) +
+                                              gemv_nw_bytes<T, NB>(K, a.norm_w != nullptr));
   __shared__ float s_red[kGemvWarps];
   __shared__ float s_scale;
   __shared__ float s_part[kGemvWarps][NB][2];
@@ -538,6 +666,14 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
     }
     cp_async_commit();
   };
+  // the norm weight and the first ring items are static: fetch them before
+  // waiting for the kernel before this one (which writes x)
+  if (nw_pre) {
+    const T* nwg = static_cast<const T*>(a.norm_w);
+    for (int64_t c = threadIdx.x; c < chunks; c += kGemvThreads)
+      cp_async_16(smem_addr(nws + c * 8), nwg + c * 8, 16u);
+  }
+  cp_async_commit();   // the oldest group: complete once the ring's first wait passes
 #pragma unroll 1
   for (int i = 0; i < kDepth - 1; ++i) issue_next();
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -547,39 +683,9 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_cc_ker
     s_epoch = ar_read_epoch(a);
     s_ar_ok = 1;
   }
-  for (int b = 0; b < NB; ++b) {
-    if (b >= a.batch) {
-      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = from_float<T>(0.f);
-      continue;
-    }
-    const T* xb = x + b * a.x_stride;
-    if (nw == nullptr) {
-      for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) xs[b * XS + i] = xb[i];
-      continue;
-    }
-    float ss = 0.f;
-    for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
-      const float v = to_float<T>(xb[i]);
-      ss = fmaf(v, v, ss);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) s_red[warp] = ss;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.f;
-      for (int w = 0; w < kGemvWarps; ++w) t += s_red[w];
-      s_scale = rsqrtf(t / static_cast<float>(K) + a.eps);
-    }
-    __syncthreads();
-    const float sc = s_scale;
-    for (int64_t i = threadIdx.x; i < K; i += kGemvThreads) {
-      const float xn = round_to<T>(to_float<T>(xb[i]) * sc);
-      xs[b * XS + i] = from_float<T>(to_float<T>(nw[i]) * xn);
-    }
-    __syncthreads();
-  }
-  __syncthreads();
+  cp_async_wait<kDepth - 1>();   // this thread's norm-weight chunks have landed
+  stage_x<T, NB, kGemvThreads, GemvShape<NB>::kStageV>(a, xs, XS, s_red, &s_scale,
+                                                        nw_pre ? nws : nullptr);
   float acc[NB], acc2[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
@@ -694,7 +800,7 @@ int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
   static size_t configured[64] = {0};  // dynamic smem allowed so far, per device
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return HELM_ERR_CUDA;
-  const size_t smem = gemv_smem_bytes<T, NB>(a.k);
+  const size_t smem = gemv_smem_bytes<T, NB>(a.k, a.norm_w != nullptr);
   // dynamic + static (the K-slice partials) shared memory of one CTA
   if (smem + sizeof(float) * GemvShape<NB>::kWarps * 16 * NB * 2 + 1024 > kGemvMaxSmem)
     return HELM_ERR_UNSUPPORTED;
@@ -721,7 +827,9 @@ int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
   const int grid_max = num_sms_current_device() * fit;
   const int unit = kMma ? 16 : 1;  // rows of one warp task
   const int64_t k_units = kMma ? a.k / 16 : a.k / 8;
-  const int64_t item_units = kMma ? (GLU ? 2 : 4) : 32 * (GLU ? 2 : 4);
+  const int64_t item_units =
+      kMma ? (GLU ? 2 : 4)
+           : 32 * (GLU ? GemvShape<NB>::kCcItemGlu : GemvShape<NB>::kCcItemPlain);
   int ks = 1;
   double best = 1e30;
   for (int c = 1; c <= kWarps; c *= 2) {
