@@ -1002,7 +1002,8 @@ def run_model(args, rank: int, world: int, dev: torch.device):
         ms = gd.decode_ms() / K
         stats = get_paging_stats()
         h2d_step = gd.h2d_bytes / K
-        plan_ms = gd.plan_seconds * 1e3 / K
+        plan_ms = (gd.plan_seconds - gd.plan_wait_seconds) * 1e3 / K
+        wait_ms = gd.plan_wait_seconds * 1e3 / K
         captures = gd.captures
         prefetch = None
         if w["cold"] > 0:
@@ -1074,7 +1075,9 @@ def run_model(args, rank: int, world: int, dev: torch.device):
                     "note": "one generate() call from a pinned host prompt to host tokens, "
                             "prefill and graph captures included"},
             "prefetch": prefetch,
-            "host_plan_ms_per_step": plan_ms, "graph_captures": captures,
+            "host_plan_ms_per_step": plan_ms,
+            "host_wait_ms_per_step": wait_ms,   # the host ahead of the GPU: waits on uploads
+            "graph_captures": captures,
             "paging": stats,
             # this library's kernels per step: per layer append + attention (+ merge) and,
             # with the fused stage, four GEMVs; plus the lm_head GEMV

@@ -194,16 +194,77 @@ class GraphDecoder:
             from .decode_stage import FusedDecodeStage
             self.stage = FusedDecodeStage(model, max_batch)
         self.h2d_bytes = 0
+        self._steady = None
 
     # -- host side of a step ------------------------------------------------------
     def _plan(self) -> None:
         """Bookkeeping of one decode token on every layer (reference order), then
         the per-layer rows, lengths and page tables, written straight into the
         pinned upload buffer of this step."""
+        ctx = self.ctx
+        if ctx.host_ev[ctx.flip] is not None:   # the buffer's previous upload is done
+            t0 = time.perf_counter()
+            ctx.host_ev[ctx.flip].synchronize()
+            self.plan_wait_seconds += time.perf_counter() - t0
+        if not self._plan_steady():
+            self._plan_full()
+        ctx.blob.copy_(ctx.host[ctx.flip], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.dev))
+        ctx.host_ev[ctx.flip] = ev
+        ctx.flip ^= 1
+
+    def _plan_steady(self) -> bool:
+        """The common step: every layer's tail page has room for the new row.
+        Then the reference's bookkeeping reduces to advancing each tail page
+        and layer by one token -- no page is allocated, the evictable set and
+        so the residency check's outcome are those of the previous step, and
+        page tables and cold-page copies are unchanged -- so only the rows and
+        lengths of the upload buffer are rewritten (the tables too when this
+        buffer was last written before the previous full plan).  False when
+        the step needs the full plan."""
+        st = self._steady
+        if st is None:
+            return False
+        kvcms, P = self.mgr.kvcms, self.ctx.P
+        layers = st["layers"]
+        if self.mgr.allocator._deferred is not None:
+            return False
+        for b, kvcm in enumerate(kvcms):
+            if kvcm._fingerprint is not st["fingerprints"][b]:
+                return False
+            for layer, n, tail in zip(layers[b], st["npages"][b], st["tails"][b]):
+                if layer._n != n or layer.tail_page is not tail or \
+                        tail.used_tokens >= tail.capacity_tokens:
+                    return False
+        rows, lens, tables = self.ctx.host_views[self.ctx.flip]
+        for b in range(len(kvcms)):
+            tails = st["tails"][b]
+            idx = tails[0].used_tokens
+            same = True
+            for layer, tail in zip(layers[b], tails):
+                u = tail.used_tokens
+                same = same and u == idx
+                tail.used_tokens = u + 1
+                layer.total_tokens += 1
+                layer._used[layer._n - 1] = u + 1
+            if same:
+                rows[:, b] = st["tail_slots"][:, b] * P + idx
+                lens[:, b] = layers[b][0].total_tokens
+            else:   # layers out of step (not produced by this decoder, but kept exact)
+                rows[:, b] = [t.slot * P + t.used_tokens - 1 for t in tails]
+                lens[:, b] = [layer.total_tokens for layer in layers[b]]
+        if st["buf_epoch"][self.ctx.flip] != st["epoch"]:
+            tables[...] = self.ctx.host_views[self.ctx.flip ^ 1][2]
+            st["buf_epoch"][self.ctx.flip] = st["epoch"]
+        for n_cold, cold_bytes in st["prefetch"]:
+            _record_prefetch(n_cold, cold_bytes)
+        self.h2d_bytes += st["h2d"]
+        return True
+
+    def _plan_full(self) -> None:
         from .kv_offload import _finish_rows
         ctx, kvcms, P = self.ctx, self.mgr.kvcms, self.ctx.P
-        if ctx.host_ev[ctx.flip] is not None:   # the buffer's previous upload is done
-            ctx.host_ev[ctx.flip].synchronize()
         rows, lens, tables = ctx.host_views[ctx.flip]
         for kvcm in kvcms:
             kvcm._begin()
@@ -218,7 +279,7 @@ class GraphDecoder:
         finally:
             _finish_rows(kvcms, self.dev)   # eviction copies queue before the replay
         stager = _stager_for(ctx.pool)
-        plans, cold_sig = [], []
+        plans, cold_sig, prefetch, h2d = [], [], [], 0
         for l in range(self.L):
             parity, n_staged, sig, groups = l & 1, 0, [], {}
             n_cold, cold_bytes = 0, 0
@@ -251,16 +312,25 @@ class GraphDecoder:
             cold_sig.append(tuple(sig))
             if n_cold:   # same accounting as the eager path: one streamed call per layer
                 _record_prefetch(n_cold, cold_bytes)
-                self.h2d_bytes += n_cold * ctx.pool.page_bytes
+                prefetch.append((n_cold, cold_bytes))
+                h2d += n_cold * ctx.pool.page_bytes
+        self.h2d_bytes += h2d
         ctx.cold_plan = plans
-        ctx.blob.copy_(ctx.host[ctx.flip], non_blocking=True)
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(self.dev))
-        ctx.host_ev[ctx.flip] = ev
-        ctx.flip ^= 1
         ptrs = tuple(p.storage.data_ptr() for p in self.mgr.allocator.pools()
                      if p.storage is not None)
         self._pending_sig = (tuple(cold_sig), ptrs)
+        # what the steady-step plan checks against (see _plan_steady)
+        epoch = (self._steady["epoch"] + 1) if self._steady is not None else 0
+        buf_epoch = self._steady["buf_epoch"] if self._steady is not None else [-1, -1]
+        buf_epoch[ctx.flip] = epoch
+        layers = [[kvcm.layers[l] for l in range(self.L)] for kvcm in kvcms]
+        tails = [[layer.tail_page for layer in ls] for ls in layers]
+        self._steady = dict(
+            epoch=epoch, buf_epoch=buf_epoch, layers=layers, tails=tails,
+            npages=[[layer._n for layer in ls] for ls in layers],
+            fingerprints=[kvcm._fingerprint for kvcm in kvcms],
+            tail_slots=np.array([[t.slot for t in ts] for ts in tails], np.int64).T.copy(),
+            prefetch=prefetch, h2d=h2d)
 
     def _step_body(self) -> None:
         ctx = self.ctx
@@ -323,6 +393,7 @@ class GraphDecoder:
         logits0 = loop.prefill(input_ids)
         for kvcm in self.mgr.kvcms:   # the replayed step reads pages only: no all-GPU window
             kvcm.migrate_contiguous_to_pages()
+        self._steady = None
         self.ctx = _GraphContext(self.mgr, B, self.Hq, self.D, self.L, self.max_len, self.dtype,
                                  self.dev)
         self.ids = torch.argmax(logits0, dim=-1, keepdim=True)
@@ -337,7 +408,8 @@ class GraphDecoder:
         # decode-phase timing (CUDA events around steps 1.., host planning time)
         self.decode_events = (torch.cuda.Event(enable_timing=True),
                               torch.cuda.Event(enable_timing=True))
-        self.plan_seconds = 0.0
+        self.plan_seconds = 0.0        # host time of the step plans, waits included
+        self.plan_wait_seconds = 0.0   # of which: waiting for an upload buffer (GPU behind)
         self.h2d_bytes = 0
         self.decode_events[0].record()
         # one eager step primes workspaces and attributes before any capture

@@ -33,19 +33,35 @@ def _close(a, b):
     assert bool(((a - b).abs() <= 2e-2 + 2 * 2 ** -7 * scale).all()), (a - b).abs().max()
 
 
+def _placement(mgr):
+    return [[(p.page_id, p.start_token, p.used_tokens, p.state) for p in layer.pages]
+            for kvcm in mgr.kvcms for layer in kvcm.layers.values()]
+
+
 @pytest.mark.parametrize("watermark", [None, 1024])
 def test_graph_decode_matches_eager(model, watermark):
+    """Same tokens and logits as the eager loop, and the same page placement
+    and paging counters afterwards: the graph path's host plan (including its
+    steady-step shortcut, which only advances tail pages) keeps the
+    reference's bookkeeping."""
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, 512, (1, 128), generator=g).cuda()
     n = 40
     cfg = KVOffloadConfig.from_model(model, page_size=16, gpu_watermark_bytes=watermark)
     mgr = KVOffloadManager(model, cfg)
-    try:
+    try:   # each path on a fresh manager, so that page ids are comparable
+        reset_paging_stats()
         toks_e, log_e = DecodeLoop(model, mgr).generate(prompt, n, keep_logits=True)
+        stats_e, place_e = get_paging_stats(), _placement(mgr)
+    finally:
+        mgr.restore()
+    mgr = KVOffloadManager(model, cfg)
+    try:
         reset_paging_stats()
         gd = GraphDecoder(model, mgr, max_len=128 + n)
         toks_g, log_g = gd.generate(prompt, n, keep_logits=True)
         stats = get_paging_stats()
+        place_g = _placement(mgr)
         runs = []
         for layer in mgr.kvcms[0].layers.values():   # host slots of a layer: few long runs
             slots = [p.slot for p in layer.pages if p.state == "CPU"]
@@ -55,6 +71,10 @@ def test_graph_decode_matches_eager(model, watermark):
     assert torch.equal(toks_e, toks_g)
     for a, b in zip(log_g, log_e):
         _close(a, b)
+    assert place_g == place_e
+    for key in ("evict_calls", "pages_evicted", "bytes_evicted", "pages_prefetched",
+                "bytes_prefetched"):
+        assert stats[key] == stats_e[key], key
     if watermark is not None:
         assert stats["pages_evicted"] > 0
         assert gd.captures >= 2   # the cold set grew during decode
