@@ -885,9 +885,12 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
     ms_mask = timed(native, max(1, steps // 2))
     ms_ref = timed(gathered, max(1, steps // 2))
     prev = os.environ.get("HELM_B200_PREFILL_KERNEL")
-    os.environ["HELM_B200_PREFILL_KERNEL"] = "mma"  # the mma.sync kernel, for comparison
-    try:
+    try:   # the other kernels, for comparison
+        os.environ["HELM_B200_PREFILL_KERNEL"] = "mma"
         ms_mma = timed(native_causal, max(1, steps // 2))
+        os.environ["HELM_B200_PREFILL_KERNEL"] = "tc1"
+        ms_tc1 = timed(native_causal, max(1, steps // 2))
+        diff_tc1 = float((native_causal().float() - b).abs().max())
     finally:
         if prev is None:
             del os.environ["HELM_B200_PREFILL_KERNEL"]
@@ -909,8 +912,12 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
                       "data": "synthetic",
                       "config": {"workload": f"prefill: 1 x {S} queries x {Hq}/{Hkv} heads over "
                                              f"{Tk} cached tokens, page {Pg}, HELM chunk mask",
-                                 "kernel": "tcgen05" if os.environ.get(
-                                     "HELM_B200_PREFILL_KERNEL") != "mma" else "mma.sync",
+                                 "kernel": {"mma": "mma.sync", "tc1": "tcgen05, one query "
+                                            "tile per CTA"}.get(
+                                     os.environ.get("HELM_B200_PREFILL_KERNEL"),
+                                     "tcgen05, two query tiles per CTA"),
+                                 "one_tile_tcgen05_kernel_ms": ms_tc1,
+                                 "max_abs_diff_one_tile_vs_gather_sdpa": diff_tc1,
                                  "mask": "recognised as chunk-causal (causal limit, no mask reads)",
                                  "ms_with_mask_read": ms_mask,
                                  "gather_sdpa_ms": ms_ref, "speedup_vs_gather_sdpa": ms_ref / ms,

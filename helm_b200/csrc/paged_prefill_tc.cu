@@ -180,17 +180,18 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 // position s to x[0 .. nvalid-1].  The dtype is chosen once per tile; a row
 // chunk that is 16-byte aligned and complete is read with 16-byte loads, all
 // issued before the first use.
+template <int N>
 __device__ __forceinline__ void add_mask_row(const PrefillArgs& a, int b, int s, int j0,
-                                             int nvalid, float (&x)[64]) {
+                                             int nvalid, float (&x)[N]) {
   const int64_t off = static_cast<int64_t>(b) * a.mask_sb + static_cast<int64_t>(s) * a.mask_sq + j0;
   if (a.mask_dtype == HELM_DTYPE_FP32) {
     const float* mp = static_cast<const float*>(a.mask) + off;
-    if (nvalid == kTcTile && (reinterpret_cast<uintptr_t>(mp) & 15) == 0) {
-      float4 v[16];
+    if (nvalid == N && (reinterpret_cast<uintptr_t>(mp) & 15) == 0) {
+      float4 v[N / 4];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __ldg(reinterpret_cast<const float4*>(mp) + i);
+      for (int i = 0; i < N / 4; ++i) v[i] = __ldg(reinterpret_cast<const float4*>(mp) + i);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < N / 4; ++i) {
         x[4 * i] += mask_log2(v[i].x);
         x[4 * i + 1] += mask_log2(v[i].y);
         x[4 * i + 2] += mask_log2(v[i].z);
@@ -198,7 +199,7 @@ __device__ __forceinline__ void add_mask_row(const PrefillArgs& a, int b, int s,
       }
     } else {
 #pragma unroll
-      for (int c = 0; c < 64; ++c)
+      for (int c = 0; c < N; ++c)
         if (c < nvalid) x[c] += mask_log2(__ldg(mp + c));
     }
     return;
@@ -208,12 +209,12 @@ __device__ __forceinline__ void add_mask_row(const PrefillArgs& a, int b, int s,
   auto cvt = [bf](uint32_t h) -> float {
     return bf ? __uint_as_float(h << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
   };
-  if (nvalid == kTcTile && (reinterpret_cast<uintptr_t>(mp) & 15) == 0) {
-    uint4 v[8];
+  if (nvalid == N && (reinterpret_cast<uintptr_t>(mp) & 15) == 0) {
+    uint4 v[N / 8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = __ldg(reinterpret_cast<const uint4*>(mp) + i);
+    for (int i = 0; i < N / 8; ++i) v[i] = __ldg(reinterpret_cast<const uint4*>(mp) + i);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < N / 8; ++i) {
       const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -223,7 +224,7 @@ __device__ __forceinline__ void add_mask_row(const PrefillArgs& a, int b, int s,
     }
   } else {
 #pragma unroll
-    for (int c = 0; c < 64; ++c)
+    for (int c = 0; c < N; ++c)
       if (c < nvalid) x[c] += mask_log2(cvt(__ldg(mp + c)));
   }
 }
@@ -603,6 +604,493 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   }
 }
 
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: relative error
+// ~2^-22, results below 2^-126 flushed to 0; probabilities that small vanish
+// in the bf16/fp16 P operand anyway).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ------------------------------------------- two query tiles per CTA (default) --
+// The same computation with two 128-row query tiles per CTA sharing every K/V
+// tile (one CTA per SM, all 512 tensor-memory columns), so that the tensor
+// core works on one tile while the other tile's rows turn scores into
+// probabilities:
+//   warps 0-3 / 4-7   softmax rows of query tile 0 / 1 (one row per thread)
+//   warp 8            one elected lane issues every tcgen05.mma: per K/V tile
+//                     S0 = Q0.K^T, S1 = Q1.K^T, then O0 += P0.V, O1 += P1.V of
+//                     the previous tile (P written meanwhile by the row warps)
+//   warp 9            TMA loads of the K/V tiles into an NS-stage ring, a stage
+//                     refilled once both P.V products of its tile completed
+// Tensor memory of query tile t: S [256t, 256t + 64), P double buffer
+// [256t + 64, 256t + 128), O [256t + 128, 256t + 128 + D).  K/V reads from L2
+// and HBM halve against the one-tile kernel (each tile serves 256 rows).
+// The row warps' common case (every key of the tile visible, no mask, no
+// soft-cap) takes each probability as one FMA and one ex2 of the raw score.
+constexpr int kT2Q = 2;
+constexpr int kT2Rows = kT2Q * kTcRows;
+constexpr int kT2SoftWarps = kT2Q * kTcSoftWarps;
+constexpr int kT2MmaWarp = kT2SoftWarps, kT2LoadWarp = kT2SoftWarps + 1;
+constexpr int kT2Threads = (kT2SoftWarps + 2) * 32;
+constexpr uint32_t kT2TmemCols = 512;
+constexpr uint32_t kT2TileCols = 256;   // tensor-memory columns of one query tile
+
+template <int D>
+struct Tc2Layout {
+  static constexpr int KS = D / 16;
+  static constexpr int kQHalf = kTcRows * 128;
+  static constexpr int kQBytes = kTcRows * D * 2;     // one query tile
+  static constexpr int kKVHalf = kTcTile * 128;
+  static constexpr int kTileBytes = kTcTile * D * 2;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kBoxes = D / 64;
+  static constexpr int NS = D <= 64 ? 8 : 4;
+  static constexpr int kBars = 2 * NS + 6 * kT2Q + 1;
+  static constexpr size_t smem_bytes() {
+    return 1024 + kT2Q * kQBytes + NS * kStageBytes + kBars * sizeof(uint64_t);
+  }
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kT2Threads, 1)
+    paged_prefill_tc2_kernel(const __grid_constant__ CUtensorMap tmap, const PrefillArgs a) {
+  using L = Tc2Layout<D>;
+  constexpr int NS = L::NS;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescQK = umma_idesc(kBf16, kTcRows, kTcTile, false);
+  constexpr uint32_t kIdescPV = umma_idesc(kBf16, kTcRows, D, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint32_t s_tmem;
+  uint8_t* smem = smem_raw + ((1024 - (smem_addr(smem_raw) & 1023)) & 1023);
+  uint8_t* sq = smem;                              // [kT2Q][kQBytes]
+  uint8_t* skv = smem + kT2Q * L::kQBytes;         // [NS][K tile | V tile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(skv + NS * L::kStageBytes);
+  uint64_t* full = bars;                 // [NS] K/V tile landed (TMA bytes)
+  uint64_t* empty = bars + NS;           // [NS] both P.V of the stage's tile completed
+  // per query tile t, at tb + 6 t: S written, S read (4 row warps), P buffer
+  // 0/1 written (4 row warps), P.V of tiles with parity 0/1 completed
+  uint64_t* tb = bars + 2 * NS;
+  uint64_t* bar_fin = tb + 6 * kT2Q;     // drain after an abandoned wait
+
+  // blockIdx.x = ((b * hkv + h) * splits + split) * row_blocks + rb (256-row blocks)
+  const int rb = blockIdx.x % a.row_blocks;
+  const int rest = blockIdx.x / a.row_blocks;
+  const int split = rest % a.splits;
+  const int pair = rest / a.splits;
+  const int b = pair / a.hkv, h = pair - (pair / a.hkv) * a.hkv;
+  const int kv_u = unit_keys(a, b, rb, kT2Rows);
+  const int n_tiles = (kv_u + kTcTile - 1) / kTcTile;
+  const int t_begin = static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
+  const int t_end = static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
+  const int n = t_end - t_begin;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int t = 0; t < kT2Q; ++t) {
+      mbar_init(tb + 6 * t + 0, 1);              // S written (tcgen05.commit)
+      mbar_init(tb + 6 * t + 1, kTcSoftWarps);   // S read
+      mbar_init(tb + 6 * t + 2, kTcSoftWarps);   // P buffer 0 written
+      mbar_init(tb + 6 * t + 3, kTcSoftWarps);   // P buffer 1 written
+      mbar_init(tb + 6 * t + 4, 1);              // P.V of even tiles completed
+      mbar_init(tb + 6 * t + 5, 1);              // P.V of odd tiles completed
+    }
+    mbar_init(bar_fin, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(&s_tmem)),
+                 "r"(kT2TmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+
+  // row of this thread (warps 0-7): query tile qt, tensor-memory lane tr
+  const int qt = warp / kTcSoftWarps;
+  const int tr = threadIdx.x - qt * kTcRows;
+  const int r = rb * kT2Rows + qt * kTcRows + tr;
+  const bool okr = warp < kT2SoftWarps && r < a.rows;
+  const int s_pos = okr ? r / a.group : 0;
+  const int qh = h * a.group + (okr ? r - s_pos * a.group : 0);
+  if (warp < kT2SoftWarps) {
+    // Q row -> its tile's slab, K-major 128-byte swizzle (as the one-tile kernel)
+    const T* qrow = static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_sb +
+                    static_cast<int64_t>(qh) * a.q_sh + static_cast<int64_t>(s_pos) * a.q_ss;
+    uint8_t* sqt = sq + qt * L::kQBytes;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (okr) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+      *reinterpret_cast<uint4*>(sqt + (c >> 3) * L::kQHalf + tr * 128 + (((c & 7) ^ (tr & 7)) << 4)) = v;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  asm volatile("griddepcontrol.launch_dependents;");
+
+  bool ok = true;
+  if (warp == kT2LoadWarp) {
+    // ================================== loads ==================================
+    const int64_t kv_rows = static_cast<int64_t>(a.hkv) * a.page_size;
+    int issued = 0;
+    if (n > 0) prefetch_tensormap(&tmap);
+    for (int i = 0; i < n; ++i) {
+      const int st = i % NS;
+      if (i >= NS && !warp_wait(&empty[st], ((i / NS) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      const int j = (t_begin + i) * kTcTile + lane * 16;
+      const bool okg = lane < 4 && j < kv_u;
+      int slot = okg ? a.page_table[static_cast<int64_t>(b) * a.pt_sb + j / a.page_size] : 0;
+      const unsigned issuing = __ballot_sync(0xffffffffu, okg);
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], __popc(issuing) * 2 * L::kBoxes * 2048);
+      __syncwarp();
+      if (okg) {
+        if (slot < 0 || slot >= a.pool_pages) {
+          report_status(HELM_DEV_BAD_PAGE);
+          slot = 0;
+        }
+        const int row_off = j - (j / a.page_size) * a.page_size;
+        const int row_k = static_cast<int>(
+            (static_cast<int64_t>(slot) * 2 * a.hkv + h) * a.page_size + row_off);
+        const int row_v = static_cast<int>(row_k + kv_rows);
+        uint8_t* kdst = skv + st * L::kStageBytes + lane * 2048;
+#pragma unroll
+        for (int hb = 0; hb < L::kBoxes; ++hb) {
+          tma_load_2d(kdst + hb * L::kKVHalf, &tmap, hb * 64, row_k, &full[st]);
+          tma_load_2d(kdst + L::kTileBytes + hb * L::kKVHalf, &tmap, hb * 64, row_v, &full[st]);
+        }
+      }
+      ++issued;
+    }
+    if (!ok) {   // the last use of every stage: wait (bounded) for its bytes to land
+      for (int i = issued > NS ? issued - NS : 0; i < issued; ++i)
+        warp_wait(&full[i % NS], (i / NS) & 1);
+    }
+  } else if (warp == kT2MmaWarp) {
+    // ================================== MMAs ===================================
+    bool mma_issued = false;
+    const uint32_t sq_addr = smem_addr(sq), skv_addr = smem_addr(skv);
+    auto do_pv = [&](int jj) -> bool {
+      const int st = jj % NS;
+      // keys of a partial tile past the unit's last key: zero their V rows
+      // (P is 0 there, but 0 x NaN would be NaN; the tile's bytes have landed)
+      const int vend = kv_u - (t_begin + jj) * kTcTile;
+      if (vend < kTcTile) {
+        uint8_t* vt = skv + st * L::kStageBytes + L::kTileBytes;
+        const int per_row = L::kBoxes * 8;
+        for (int idx = lane; idx < (kTcTile - vend) * per_row; idx += 32) {
+          const int row = vend + idx / per_row, c = idx - (idx / per_row) * per_row;
+          *reinterpret_cast<uint4*>(vt + (c >> 3) * L::kKVHalf + row * 128 + (c & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+      }
+      const uint32_t vaddr = skv_addr + st * L::kStageBytes + L::kTileBytes;
+      for (int t = 0; t < kT2Q; ++t) {
+        uint64_t* tbt = tb + 6 * t;
+        if (!warp_wait(tbt + 2 + (jj & 1), (jj >> 1) & 1)) return false;
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t cols = tmem + t * kT2TileCols;
+#pragma unroll
+          for (int kt = 0; kt < kTcTile / 16; ++kt)
+            umma_ts(cols + kColO, cols + kColP + (jj & 1) * 32 + kt * 8,
+                    umma_desc(vaddr + kt * 2048, L::kKVHalf, 1024), kIdescPV,
+                    (jj > 0 || kt > 0) ? 1u : 0u);
+          umma_commit(tbt + 4 + (jj & 1));
+        }
+        __syncwarp();
+      }
+      if (lane == 0) umma_commit(&empty[st]);
+      __syncwarp();
+      return true;
+    };
+    for (int j = 0; j < n && ok; ++j) {
+      const int st = j % NS;
+      if (!warp_wait(&full[st], (j / NS) & 1)) {
+        ok = false;
+        break;
+      }
+      const uint32_t kaddr = skv_addr + st * L::kStageBytes;
+      for (int t = 0; t < kT2Q; ++t) {
+        uint64_t* tbt = tb + 6 * t;
+        if (j > 0 && !warp_wait(tbt + 1, (j - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t qaddr = sq_addr + t * L::kQBytes;
+#pragma unroll
+          for (int kk = 0; kk < L::KS; ++kk) {
+            const uint32_t off = (kk & 3) * 32;  // 16 elements = 32 B along K
+            umma_ss(tmem + t * kT2TileCols + kColS,
+                    umma_desc(qaddr + (kk >> 2) * L::kQHalf + off, 16, 1024),
+                    umma_desc(kaddr + (kk >> 2) * L::kKVHalf + off, 16, 1024), kIdescQK,
+                    kk > 0 ? 1u : 0u);
+          }
+          umma_commit(tbt + 0);
+        }
+        mma_issued = true;
+        __syncwarp();
+      }
+      if (ok && j > 0 && !do_pv(j - 1)) ok = false;
+    }
+    if (ok && n > 0) {
+      ok = do_pv(n - 1);
+      // tensor memory must be idle before it is released
+      for (int t = 0; ok && t < kT2Q; ++t)
+        ok = warp_wait(tb + 6 * t + 4 + ((n - 1) & 1), ((n - 1) >> 1) & 1);
+    }
+    if (!ok && mma_issued) {
+      // a wait was abandoned (reported): wait (bounded) for the MMAs issued
+      if (lane == 0) umma_commit(bar_fin);
+      __syncwarp();
+      warp_wait(bar_fin, 0);
+    }
+  } else {
+    // ================================ row warps ================================
+    uint64_t* tbt = tb + 6 * qt;
+    const uint32_t lane_off = static_cast<uint32_t>(32 * (warp & 3)) << 16;
+    const uint32_t cols = tmem + lane_off + qt * kT2TileCols;
+    const int kv_len = min(a.kv_lens[b], a.max_pages * a.page_size);
+    const int pos = kv_len - a.q_len + s_pos;  // absolute position of this row's query
+    float m_ref = -INFINITY, l = 0.f;
+    for (int j = 0; j < n; ++j) {
+      if (!warp_wait(tbt + 0, j & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t ra[32], rb2[32];
+      tmem_ld32(cols + kColS, ra);
+      tmem_ld32(cols + kColS + 32, rb2);
+      tmem_wait_ld(ra);
+      tmem_wait_ld(rb2);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tbt + 1);  // S may now be overwritten
+
+      const int j0 = (t_begin + j) * kTcTile;
+      const int vend = kv_u - j0;
+      float x[64];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        x[c] = __uint_as_float(ra[c]);
+        x[32 + c] = __uint_as_float(rb2[c]);
+      }
+      const bool all_in = okr && vend >= kTcTile && (!a.causal || j0 + kTcTile - 1 <= pos);
+      // Most tiles: every key of every row of the warp is visible, no mask and
+      // no soft-cap.  Then the row max is taken on the raw scores (the scale is
+      // positive, so the order and the rounded scaled max are the same) and
+      // each probability is one FMA and one exp2: ex2(x * scale - m).
+      const bool fast = a.softcap <= 0.f && a.mask == nullptr && a.scale_log2 > 0.f &&
+                        __all_sync(0xffffffffu, all_in);
+      float mx = -INFINITY;
+      if (fast) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) mx = fmaxf(mx, x[c]);
+        mx *= a.scale_log2;
+      } else {
+        if (a.softcap > 0.f) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c)
+            x[c] = a.softcap * tanhf(x[c] * a.scale / a.softcap) * kLog2e;
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) x[c] *= a.scale_log2;
+        }
+        if (a.mask != nullptr && okr)
+          add_mask_row(a, b, s_pos, j0, all_in ? kTcTile : min(vend, kTcTile), x);
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const bool in = all_in || (okr && c < vend && (!a.causal || j0 + c <= pos));
+          x[c] = in ? x[c] : -INFINITY;
+          mx = fmaxf(mx, x[c]);
+        }
+      }
+      // reference max: moves only when the row's max grows by more than 2^8
+      const bool need = mx > m_ref + kRescaleLog2 || (m_ref == -INFINITY && mx > -INFINITY);
+      const float m_new = need ? mx : m_ref;
+      const float alpha = need ? exp2f(m_ref - m_new) : 1.f;  // 0 while m_ref is -inf
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      m_ref = m_new;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O holds the previous tiles: rescale once P.V of tile j-1 completed
+        if (!warp_wait(tbt + 4 + ((j - 1) & 1), ((j - 1) >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(cols + kColO + c0, o);
+          tmem_wait_ld(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(cols + kColO + c0, o);
+        }
+        tmem_wait_st();
+      }
+      // P buffer (j & 1) was last read by P.V of tile j-2
+      if (j >= 2 && !warp_wait(tbt + 4 + (j & 1), ((j - 2) >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sum = 0.f;
+      uint32_t pk[32];
+      if (fast) {
+        const float sl = a.scale_log2;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = ex2_approx(fmaf(x[2 * c], sl, -m_use));
+          const float p1 = ex2_approx(fmaf(x[2 * c + 1], sl, -m_use));
+          sum += p0 + p1;
+          pk[c] = MmaOp<T>::pack(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = exp2f(x[2 * c] - m_use), p1 = exp2f(x[2 * c + 1] - m_use);
+          sum += p0 + p1;
+          pk[c] = MmaOp<T>::pack(p0, p1);
+        }
+      }
+      l = l * alpha + sum;
+      tmem_st32(cols + kColP + (j & 1) * 32, pk);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tbt + 2 + (j & 1));
+    }
+    if (ok && n > 0) {
+      ok = warp_wait(tbt + 4 + ((n - 1) & 1), ((n - 1) >> 1) & 1);
+      tc_fence_after();
+    }
+    if (ok) {
+      if (a.splits == 1) {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = static_cast<T*>(a.out) + static_cast<int64_t>(b) * a.o_sb +
+                  static_cast<int64_t>(qh) * a.o_sh + static_cast<int64_t>(s_pos) * a.o_ss;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (n > 0) {
+            tmem_ld32(cols + kColO + c0, o);
+            tmem_wait_ld(o);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            pk[e] = MmaOp<T>::pack(__uint_as_float(o[2 * e]) * inv,
+                                   __uint_as_float(o[2 * e + 1]) * inv);
+          if (okr) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              *reinterpret_cast<uint4*>(orow + c0 + 8 * e) =
+                  make_uint4(pk[4 * e], pk[4 * e + 1], pk[4 * e + 2], pk[4 * e + 3]);
+          }
+        }
+      } else {
+        const int64_t part = (static_cast<int64_t>(pair) * a.row_blocks + rb) * a.splits + split;
+        const int64_t rec = part * kT2Rows + qt * kTcRows + tr;
+        float* po = a.part_o + rec * D;
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t o[32];
+          if (n > 0) {
+            tmem_ld32(cols + kColO + c0, o);
+            tmem_wait_ld(o);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = 0u;
+          }
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            *reinterpret_cast<float4*>(po + c0 + 4 * e) =
+                make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                            __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+        }
+        *reinterpret_cast<float2*>(a.part_ml + rec * 2) = make_float2(m_ref, l);
+      }
+    }
+  }
+  // all tensor-memory traffic of the CTA is complete: release the columns
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kT2TmemCols)
+                 : "memory");
+  }
+}
+
+template <typename T, int D>
+int launch_prefill_tc2(PrefillArgs a, const void* pool, int64_t pool_rows, int max_kv_len,
+                       void* workspace, int64_t workspace_bytes, cudaStream_t stream) {
+  static bool configured[64][2] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HELM_ERR_CUDA;
+  if (!configured[dev][D == 128]) {
+    if (cudaFuncSetAttribute(paged_prefill_tc2_kernel<T, D>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Tc2Layout<D>::smem_bytes())) != cudaSuccess)
+      return HELM_ERR_CUDA;
+    configured[dev][D == 128] = true;
+  }
+  const PrefillPlan plan =
+      plan_prefill(a.batch, a.q_len, a.hq, a.hkv, D, max_kv_len, 1, kT2Rows);
+  if (workspace_bytes < plan.total()) return HELM_ERR_WORKSPACE;
+  if (plan.total() > 0 && workspace == nullptr) return HELM_ERR_WORKSPACE;
+  a.row_blocks = plan.row_blocks;
+  a.splits = plan.splits;
+  uint8_t* wsp = static_cast<uint8_t*>(workspace);
+  a.part_o = plan.splits > 1 ? reinterpret_cast<float*>(wsp) : nullptr;
+  a.part_ml = plan.splits > 1 ? reinterpret_cast<float*>(wsp + plan.o_bytes) : nullptr;
+  const int64_t grid = plan.units * plan.splits;
+  if (grid <= 0) return HELM_OK;
+  if (grid >= (int64_t(1) << 31)) return HELM_ERR_UNSUPPORTED;
+  CUtensorMap map;
+  if (!encode_pool_map<T, D>(pool, pool_rows, &map)) return HELM_ERR_CUDA;
+  paged_prefill_tc2_kernel<T, D><<<static_cast<unsigned>(grid), kT2Threads,
+                                   Tc2Layout<D>::smem_bytes(), stream>>>(map, a);
+  if (cudaGetLastError() != cudaSuccess) return HELM_ERR_CUDA;
+  if (plan.splits == 1) return HELM_OK;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(plan.units),
+                     static_cast<unsigned>((kT2Rows * D / 4 + kPfMergeThreads - 1) / kPfMergeThreads));
+  cfg.blockDim = dim3(kPfMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, merge_prefill_splits_kernel<T, D, kT2Rows>, a) != cudaSuccess)
+    return HELM_ERR_CUDA;
+  return HELM_OK;
+}
+
 template <typename T, int D>
 int tc_ctas_per_sm() {
   static int cached[64] = {0};
@@ -662,28 +1150,34 @@ int launch_prefill_tc(PrefillArgs a, const void* pool, int64_t pool_rows, int ma
   return HELM_OK;
 }
 
-// Which kernel serves a call: the tcgen05 one unless HELM_B200_PREFILL_KERNEL
-// is "mma" (the mma.sync kernel) or the query / output rows are not 16-byte
-// aligned (the tcgen05 kernel moves whole 16-byte chunks of a row).
-bool prefill_use_tc(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss, const void* out,
-                    int64_t o_sb, int64_t o_sh, int64_t o_ss) {
+// Which kernel serves a call: 0 the mma.sync kernel, 1 the one-tile tcgen05
+// kernel, 2 the two-tile tcgen05 kernel (the default).  HELM_B200_PREFILL_KERNEL
+// = "mma" / "tc1" selects the first two; query / output rows that are not
+// 16-byte aligned take the mma.sync kernel (the tcgen05 kernels move whole
+// 16-byte chunks of a row).
+int prefill_kernel_choice(const void* q, int64_t q_sb, int64_t q_sh, int64_t q_ss,
+                          const void* out, int64_t o_sb, int64_t o_sh, int64_t o_ss) {
   const char* env = std::getenv("HELM_B200_PREFILL_KERNEL");
-  if (env != nullptr && std::strcmp(env, "mma") == 0) return false;
+  if (env != nullptr && std::strcmp(env, "mma") == 0) return 0;
   const bool q_ok = (reinterpret_cast<uintptr_t>(q) & 15) == 0 && q_sb % 8 == 0 &&
                     q_sh % 8 == 0 && q_ss % 8 == 0;
   const bool o_ok = out == nullptr || ((reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
                                        o_sb % 8 == 0 && o_sh % 8 == 0 && o_ss % 8 == 0);
-  return q_ok && o_ok;
+  if (!(q_ok && o_ok)) return 0;
+  return (env != nullptr && std::strcmp(env, "tc1") == 0) ? 1 : 2;
 }
 
 template <typename T>
-int prefill_tc_dispatch(int head_dim, const PrefillArgs& a, const void* pool, int64_t rows,
-                        int max_kv_len, void* ws, int64_t ws_bytes, cudaStream_t s) {
+int prefill_tc_dispatch(int kernel, int head_dim, const PrefillArgs& a, const void* pool,
+                        int64_t rows, int max_kv_len, void* ws, int64_t ws_bytes,
+                        cudaStream_t s) {
   switch (head_dim) {
     case 64:
-      return launch_prefill_tc<T, 64>(a, pool, rows, max_kv_len, ws, ws_bytes, s);
+      return kernel == 2 ? launch_prefill_tc2<T, 64>(a, pool, rows, max_kv_len, ws, ws_bytes, s)
+                         : launch_prefill_tc<T, 64>(a, pool, rows, max_kv_len, ws, ws_bytes, s);
     case 128:
-      return launch_prefill_tc<T, 128>(a, pool, rows, max_kv_len, ws, ws_bytes, s);
+      return kernel == 2 ? launch_prefill_tc2<T, 128>(a, pool, rows, max_kv_len, ws, ws_bytes, s)
+                         : launch_prefill_tc<T, 128>(a, pool, rows, max_kv_len, ws, ws_bytes, s);
     default:
       return HELM_ERR_UNSUPPORTED;
   }
@@ -720,7 +1214,10 @@ extern "C" int64_t helm_paged_prefill_workspace_bytes(int batch, int q_len, int 
   const int64_t w_tc =
       plan_prefill(batch, q_len, num_q_heads, num_kv_heads, head_dim, max_kv_len, c_tc, kTcRows)
           .total();
-  return std::max(w_mma, w_tc);
+  const int64_t w_tc2 =
+      plan_prefill(batch, q_len, num_q_heads, num_kv_heads, head_dim, max_kv_len, 1, kT2Rows)
+          .total();
+  return std::max(std::max(w_mma, w_tc), w_tc2);
 }
 
 extern "C" int helm_paged_prefill_attention(
@@ -793,19 +1290,19 @@ extern "C" int helm_paged_prefill_attention(
   a.scale_log2 = scale * kLog2e;
   a.softcap = softcap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool tc = prefill_use_tc(q, q_stride_b, q_stride_h, q_stride_s, out, out_stride_b,
-                                 out_stride_h, out_stride_s);
+  const int kernel = prefill_kernel_choice(q, q_stride_b, q_stride_h, q_stride_s, out,
+                                           out_stride_b, out_stride_h, out_stride_s);
   int rc;
   if (dtype == HELM_DTYPE_BF16)
-    rc = tc ? prefill_tc_dispatch<__nv_bfloat16>(head_dim, a, kv_pool, pool_rows, max_kv_len,
-                                                 workspace, workspace_bytes, s)
-            : prefill_dispatch<__nv_bfloat16>(head_dim, a, kv_pool, pool_rows, max_kv_len,
-                                              workspace, workspace_bytes, s);
+    rc = kernel ? prefill_tc_dispatch<__nv_bfloat16>(kernel, head_dim, a, kv_pool, pool_rows,
+                                                     max_kv_len, workspace, workspace_bytes, s)
+                : prefill_dispatch<__nv_bfloat16>(head_dim, a, kv_pool, pool_rows, max_kv_len,
+                                                  workspace, workspace_bytes, s);
   else
-    rc = tc ? prefill_tc_dispatch<__half>(head_dim, a, kv_pool, pool_rows, max_kv_len, workspace,
-                                          workspace_bytes, s)
-            : prefill_dispatch<__half>(head_dim, a, kv_pool, pool_rows, max_kv_len, workspace,
-                                       workspace_bytes, s);
+    rc = kernel ? prefill_tc_dispatch<__half>(kernel, head_dim, a, kv_pool, pool_rows, max_kv_len,
+                                              workspace, workspace_bytes, s)
+                : prefill_dispatch<__half>(head_dim, a, kv_pool, pool_rows, max_kv_len, workspace,
+                                           workspace_bytes, s);
   if (rc == HELM_ERR_CUDA) set_last_cuda_error(cudaGetLastError());
   return rc;
 }

@@ -296,6 +296,57 @@ def _is_chunk_causal(attention_mask: torch.Tensor, mask: torch.Tensor, lens: np.
     return verdict
 
 
+def _kernel_prefill(q, pool, slots, kl, lens, T: int, P: int, scale: float, attention_mask,
+                    mask, softcap):
+    """helm_paged_prefill_attention when the chunk's mask lets the kernel serve
+    it: HELM's chunk-causal mask (recognised, then applied as the causal limit
+    without reading it), no mask, or a soft-cap (the mask read); None
+    otherwise (see _prefill_dense_pages for the environment switch)."""
+    Hkv = pool.shape[2]
+    native = (pool.dtype == q.dtype and _capi.prefill_supported(q.dtype, q.shape[-1], P)
+              and (mask is None or (mask.dim() == 4 and mask.shape[1] == 1
+                                    and mask.shape[2] == q.shape[2] and mask.shape[3] == T
+                                    and mask.dtype in (torch.float32, torch.bfloat16,
+                                                       torch.float16))))
+    choice = os.environ.get("HELM_B200_NATIVE_PREFILL")
+    use_kernel = causal = False
+    if native and (choice != "0" or softcap is not None):
+        causal = mask is not None and _is_chunk_causal(attention_mask, mask, lens, q.shape[2])
+        use_kernel = softcap is not None or choice == "1" or mask is None or causal
+    if not use_kernel:
+        return None
+    return _capi.paged_prefill_attention(q, pool, slots, kl, num_kv_heads=Hkv, page_size=P,
+                                         scale=scale, max_kv_len=T,
+                                         mask=None if causal else mask, causal=causal,
+                                         softcap=softcap)
+
+
+def _prefill_first_chunk(q, k, v, attention_mask, scale: float, softcap):
+    """The first chunk of a prompt (no cached keys before it) on the prefill
+    kernel, from the chunk's own K/V laid out as a small page pool (one copy
+    of the chunk's K/V, 64-token pages): the same arithmetic whether or not
+    the pages just appended stayed resident, so offload does not change the
+    result.  None when the mask is one the kernel does not serve."""
+    B, Hkv, S, D = k.shape
+    P = 64
+    if not _capi.prefill_supported(q.dtype, D, P) or k.dtype != q.dtype:
+        return None
+    npg = -(-S // P)
+    pad = npg * P - S
+
+    def pages(t):   # [B, Hkv, S, D] -> [B, npg, Hkv, P, D]
+        if pad:
+            t = F.pad(t, (0, 0, 0, pad))
+        return t.view(B, Hkv, npg, P, D).permute(0, 2, 1, 3, 4)
+    pool = torch.stack([pages(k), pages(v)], dim=2).reshape(B * npg, 2, Hkv, P, D)
+    dev = q.device
+    slots = torch.arange(B * npg, dtype=torch.int32, device=dev).view(B, npg)
+    lens = np.full(B, S, np.int32)
+    kl = torch.full((B,), S, dtype=torch.int32, device=dev)
+    mask = None if attention_mask is None else attention_mask[..., :S].to(device=dev)
+    return _kernel_prefill(q, pool, slots, kl, lens, S, P, scale, attention_mask, mask, softcap)
+
+
 def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
                          attention_mask: Optional[torch.Tensor],
                          softcap: Optional[float] = None) -> Optional[torch.Tensor]:
@@ -331,23 +382,10 @@ def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
     slots = torch.from_numpy(np.ascontiguousarray(t.slots)).pin_memory().to(dev, non_blocking=True)
     kl = torch.from_numpy(lens).pin_memory().to(dev, non_blocking=True)
     mask = None if attention_mask is None else attention_mask[..., :T].to(device=dev)
-    native = (pool.storage.dtype == q.dtype and _capi.prefill_supported(q.dtype, q.shape[-1], P)
-              and (mask is None or (mask.dim() == 4 and mask.shape[1] == 1
-                                    and mask.shape[2] == q.shape[2] and mask.shape[3] == T
-                                    and mask.dtype in (torch.float32, torch.bfloat16,
-                                                       torch.float16))))
-    choice = os.environ.get("HELM_B200_NATIVE_PREFILL")
-    use_kernel = causal = False
-    if native and (choice != "0" or softcap is not None):
-        causal = mask is not None and _is_chunk_causal(attention_mask, mask, lens, q.shape[2])
-        use_kernel = softcap is not None or choice == "1" or mask is None or causal
-    if use_kernel:
-        return _capi.paged_prefill_attention(q, pool.storage, slots, kl, num_kv_heads=Hkv,
-                                             page_size=P, scale=scale, max_kv_len=T,
-                                             mask=None if causal else mask, causal=causal,
-                                             softcap=softcap)
-    if softcap is not None:
-        return None
+    out = _kernel_prefill(q, pool.storage, slots, kl, lens, T, P, scale, attention_mask, mask,
+                          softcap)
+    if out is not None or softcap is not None:
+        return out
     k, v = _capi.gather_kv(pool.storage, slots, kl, T, num_kv_heads=Hkv, page_size=P)
     if k.dtype != q.dtype:
         k, v = k.to(q.dtype), v.to(q.dtype)
@@ -376,6 +414,13 @@ def _prefill(attn_self, kvcms, q, k, v, attention_mask, scale, softcap=None):
     if any(past > 0 for past in past_lengths):
         return _stream_prefill_batched(kvcms, q, attn_self.layer_idx, scale, attention_mask,
                                        softcap)
+    # first chunk: the chunk-prefill kernel (HELM's chunk-causal mask, no mask,
+    # or a soft-cap); the reference's dense attention over k, v for other
+    # masks (kv_offload.py:387-395)
+    if q.device.type == "cuda":
+        out = _prefill_first_chunk(q, k, v, attention_mask, scale, softcap)
+        if out is not None:
+            return out
     groups = q.shape[1] // k.shape[1]
     if softcap is None:
         return F.scaled_dot_product_attention(q, k, v, attn_mask=attention_mask, scale=scale,

@@ -1,6 +1,7 @@
 """Parity of the CUDA chunk-prefill attention (helm_paged_prefill_attention,
-through the C ABI) with the CPU oracle, for both of its kernels: the tcgen05
-one (default) and the mma.sync one (HELM_B200_PREFILL_KERNEL=mma).
+through the C ABI) with the CPU oracle, for each of its kernels: the tcgen05
+kernel with two query tiles per CTA (default), the one-tile tcgen05 kernel
+(HELM_B200_PREFILL_KERNEL=tc1) and the mma.sync one (=mma).
 
 A prefill chunk is, row by row, the reference's streaming attention
 (helm/runtime/kv_cache.py:469-555) for one query with the mask row of that
@@ -97,7 +98,7 @@ CASES = [
 ]
 
 
-@pytest.fixture(params=["tc", "mma"])
+@pytest.fixture(params=["tc", "tc1", "mma"])
 def kernel(request, monkeypatch):
     monkeypatch.setenv("HELM_B200_PREFILL_KERNEL", request.param)
     return request.param
