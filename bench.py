@@ -222,6 +222,16 @@ def _split_inputs(rank: int, world: int, dev: torch.device):
     return q, pool, pt, kl, b - a
 
 
+def _raise_on_status(status: int, world: int, dev: torch.device) -> None:
+    """Raises on every rank when any rank's device status word reports an error
+    (so that no rank goes on to a collective the failed one will not join)."""
+    t = torch.tensor([status], dtype=torch.int64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    if int(t.item()) != 0:
+        raise RuntimeError(f"device status {status} on this rank, {int(t.item())} on some rank")
+
+
 def _timed(fn, steps: int, world: int, dev: torch.device, stream, clocks_soak: bool):
     """Device time of `steps` calls of fn (CUDA events on `stream`, barrier and
     synchronize on both sides), max over ranks; optional nvidia-smi sampling."""
@@ -232,12 +242,24 @@ def _timed(fn, steps: int, world: int, dev: torch.device, stream, clocks_soak: b
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = None
+    n_soak = 0
+    if clocks_soak:
+        # keep the GPU under the same load for ~0.6 s so that nvidia-smi sees it; the
+        # count of soak calls is agreed by all ranks (a call may hold a collective, so
+        # every rank must make the same number of them)
+        t0 = time.perf_counter()
+        fn(5)
+        torch.cuda.synchronize(dev)
+        per = max(time.perf_counter() - t0, 1e-4)
+        t = torch.tensor([min(2000, int(0.6 / per) + 1)], dtype=torch.int64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        n_soak = int(t.item())
+        barrier()
     with ClockSampler(dev.index) as sampler:
-        if clocks_soak:   # keep the GPU under the same load for ~0.6 s so nvidia-smi sees it
-            t_soak = time.perf_counter()
-            while time.perf_counter() - t_soak < 0.6:
-                fn(5)
-                torch.cuda.synchronize(dev)
+        for _ in range(n_soak):
+            fn(5)
+        torch.cuda.synchronize(dev)
         ev0.record(stream)
         fn(steps)
         ev1.record(stream)
@@ -361,8 +383,7 @@ def run_b200(args, rank: int, world: int, dev: torch.device):
     finally:
         if px is not None:
             px.close()
-    if status != 0:
-        raise RuntimeError(f"device status {status}")
+    _raise_on_status(status, world, dev)
 
     model = None
     if not args.no_model_block:
@@ -601,8 +622,7 @@ def _tp_decode(name: str, args, rank: int, world: int, dev: torch.device, steps:
         tp.close()
         del tp, shard
         torch.cuda.empty_cache()
-    if status != 0:
-        raise RuntimeError(f"device status {status}")
+    _raise_on_status(status, world, dev)
     hbm, peak_src = _peaks()
     step_bytes = wbytes + kv_bytes
     achieved = step_bytes / (ms / 1e3) / 1e9
