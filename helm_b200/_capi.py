@@ -198,9 +198,39 @@ def reset_workspace(device: torch.device) -> None:
         ws.buf.zero_()
 
 
+_ws_bytes_cache: dict = {}
+
+
 def decode_workspace_bytes(device: torch.device, batch: int, hq: int, hkv: int, d: int) -> int:
-    with torch.cuda.device(device):
-        return int(lib().helm_paged_decode_workspace_bytes(batch, hq, hkv, d))
+    """Workspace bytes of a decode call (depends on the device's SM count: cached)."""
+    key = (device.index, batch, hq, hkv, d)
+    v = _ws_bytes_cache.get(key)
+    if v is None:
+        with torch.cuda.device(device):
+            v = _ws_bytes_cache[key] = int(lib().helm_paged_decode_workspace_bytes(batch, hq, hkv,
+                                                                                  d))
+    return v
+
+
+class _on_device:
+    """torch.cuda.device(dev), skipped when dev is current already (the common
+    case; entering the context costs several microseconds per call)."""
+    __slots__ = ("dev", "ctx")
+
+    def __init__(self, dev: torch.device):
+        self.dev = dev
+        self.ctx = None
+
+    def __enter__(self):
+        if torch.cuda.current_device() != self.dev.index:
+            self.ctx = torch.cuda.device(self.dev)
+            self.ctx.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.__exit__(*exc)
+        return False
 
 
 # ------------------------------------------------------------------- wrappers --
@@ -244,7 +274,7 @@ def paged_decode_attention(q: torch.Tensor, pool: torch.Tensor, page_table: torc
             mask = mask.contiguous()
         mask_ptr, mask_dt = mask.data_ptr(), helm_dtype(mask.dtype)
         mask_sb = mask.stride(0) if mask.shape[0] > 1 else 0
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_paged_decode_attention(
             q.data_ptr(), q.stride(0), q.stride(1),
             pool.data_ptr(), pool.shape[0],
@@ -299,7 +329,7 @@ def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, page_table: tor
         mask_sb = mask.stride(0) if mask.shape[0] > 1 else 0
         mask_sq = mask.stride(2)
     dt = helm_dtype(q.dtype)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         ws_bytes = int(lib().helm_paged_prefill_workspace_bytes(B, S, Hq, num_kv_heads, D, dt,
                                                                 int(max_kv_len)))
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
@@ -344,7 +374,7 @@ def kv_append(*, k: torch.Tensor, v: torch.Tensor, pool: Optional[torch.Tensor],
         raise HelmError("cos/sin must have a unit stride on the head dim")
     if slot_rows is not None and slot_rows.dtype != torch.int64:
         raise HelmError("slot_rows must be int64")
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_kv_append(
             _ptr(q), q.stride(0) if q is not None else 0, q.stride(1) if q is not None else 0,
             k.data_ptr(), k.stride(0), k.stride(1),
@@ -386,7 +416,7 @@ def gather_kv(pool: torch.Tensor, page_table: torch.Tensor, kv_lens: torch.Tenso
     dev = pool.device
     k = torch.empty(B, num_kv_heads, t_max, D, dtype=pool.dtype, device=dev)
     v = torch.empty_like(k)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_gather_kv(pool.data_ptr(), pool.shape[0], page_table.data_ptr(),
                                   page_table.stride(0), page_table.shape[1], kv_lens.data_ptr(),
                                   k.data_ptr(), v.data_ptr(), B, num_kv_heads, D, page_size,
@@ -409,7 +439,7 @@ def merge_attention_states(o_parts: torch.Tensor, lse_parts: torch.Tensor,
     dev = o_parts.device
     out = torch.empty(o_parts.shape[1:], dtype=out_dtype, device=dev)
     lse = torch.empty(lse_parts.shape[1:], dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_merge_attention_states(
             o_parts.data_ptr(), helm_dtype(o_parts.dtype), o_parts.stride(0),
             lse_parts.data_ptr(), lse_parts.stride(0), R, rows, D,
@@ -480,7 +510,7 @@ def seq_exchange_merge(bufs: list, rank: int, o_part: torch.Tensor, lse_part: to
         raise HelmError("lse_out must be fp32 [rows]")
     dev = o_part.device
     arr = (ctypes.c_void_p * len(bufs))(*bufs)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_seq_exchange_merge(arr, rank, len(bufs), o_part.data_ptr(),
                                            lse_part.data_ptr(), rows, D, out.data_ptr(),
                                            helm_dtype(out.dtype), _ptr(lse_out),
@@ -526,7 +556,7 @@ def decode_gemv(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor,
     if residual is not None and (residual.shape != out.shape or residual.stride(1) != 1):
         raise HelmError("decode_gemv: residual must match out")
     dev = x.device
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_decode_gemv(
             x.data_ptr(), x.stride(0), _ptr(norm_w), float(eps), w.data_ptr(), _ptr(w2), N, K,
             _ptr(residual), residual.stride(0) if residual is not None else 0,
@@ -559,7 +589,7 @@ def decode_gemv_allreduce(bufs: list, rank: int, x: torch.Tensor, w: torch.Tenso
         raise HelmError("decode_gemv_allreduce: residual must match out")
     dev = x.device
     arr = (ctypes.c_void_p * len(bufs))(*bufs)
-    with torch.cuda.device(dev):
+    with _on_device(dev):
         rc = lib().helm_decode_gemv_allreduce(
             arr, rank, len(bufs), x.data_ptr(), x.stride(0), w.data_ptr(), N, K, _ptr(residual),
             residual.stride(0) if residual is not None else 0, out.data_ptr(), out.stride(0), B,

@@ -91,7 +91,12 @@ __device__ __forceinline__ uint2* slot_ptr(unsigned char* buf, int64_t stride, i
 }
 
 __global__ void __launch_bounds__(128) seq_exchange_merge_kernel(PeerExchangeArgs a) {
+  // Launched as a programmatic dependent: placed while the kernel before it
+  // (the decode kernel and its merge, which write o_part / lse_part) finishes;
+  // everything below waits for it.  The next call's decode kernel may be
+  // placed now (it reads no exchange state and writes only after waiting).
   asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int c = blockIdx.x;
   const int D = a.head_dim;
   const int64_t r0 = (int64_t)c * a.chunk_rows;
@@ -318,8 +323,16 @@ extern "C" int helm_seq_exchange_merge(void* const* bufs, int rank, int world, c
   a.head_dim = head_dim;
   a.chunk_rows = g.chunk_rows;
   a.out_dtype = out_dtype;
-  seq_exchange_merge_kernel<<<g.chunks, 128, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g.chunks);
+  cfg.blockDim = dim3(128);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, seq_exchange_merge_kernel, a);
   if (e != cudaSuccess) {
     set_last_cuda_error(e);
     return HELM_ERR_CUDA;
