@@ -903,6 +903,15 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
     diff_mask = float((native().float() - b).abs().max())
     ms = timed(native_causal, steps)
     ms_mask = timed(native, max(1, steps // 2))
+    # a left-padded prompt: HELM's padding mask as a first visible key
+    pad = Tk // 32
+    starts = torch.tensor([pad], dtype=torch.int32, device=dev)
+
+    def native_padded():
+        return _capi.paged_prefill_attention(q, pool, table, lens, num_kv_heads=Hkv, page_size=Pg,
+                                             scale=scale, max_kv_len=Tk, causal=True,
+                                             kv_starts=starts)
+    ms_pad = timed(native_padded, max(1, steps // 2))
     ms_ref = timed(gathered, max(1, steps // 2))
     prev = os.environ.get("HELM_B200_PREFILL_KERNEL")
     try:   # the other kernels, for comparison
@@ -940,6 +949,9 @@ def run_prefill(args, rank: int, world: int, dev: torch.device):
                                  "max_abs_diff_one_tile_vs_gather_sdpa": diff_tc1,
                                  "mask": "recognised as chunk-causal (causal limit, no mask reads)",
                                  "ms_with_mask_read": ms_mask,
+                                 "left_padded_ms": ms_pad,
+                                 "left_padded_note": f"first {pad} keys padded, given as a key "
+                                                     "start (no mask reads)",
                                  "gather_sdpa_ms": ms_ref, "speedup_vs_gather_sdpa": ms_ref / ms,
                                  "mma_sync_kernel_ms": ms_mma,
                                  "max_abs_diff_vs_gather_sdpa": diff,

@@ -60,7 +60,7 @@ _SIGNATURES = {
         _P, _I64, _I64, _I64,      # q, strides (b, h, s)
         _P, _I64,                  # pool, pool_pages
         _P, _I64, _I,              # page_table, pt_stride_b, max_pages
-        _P,                        # kv_lens
+        _P, _P,                    # kv_lens, kv_starts
         _P, _I, _I64, _I64,        # mask, mask_dtype, mask strides (b, q)
         _P, _I64, _I64, _I64,      # out, strides (b, h, s)
         _P, _I64,                  # workspace, bytes
@@ -294,14 +294,17 @@ def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, page_table: tor
                             kv_lens: torch.Tensor, *, num_kv_heads: int, page_size: int,
                             scale: float, max_kv_len: int, mask: Optional[torch.Tensor] = None,
                             causal: bool = False, softcap: Optional[float] = None,
+                            kv_starts: Optional[torch.Tensor] = None,
                             out: Optional[torch.Tensor] = None, stream=None) -> torch.Tensor:
     """Chunk-prefill attention over a page pool (the chunk's K/V already in it).
 
     q [B, Hq, S, D] (any strides, unit dim stride); pool [slots, 2, Hkv, P, D];
     page_table int32 [B, max_pages]; kv_lens int32 [B] (query i of sequence b
     sits at position kv_lens[b] - S + i); mask additive [B or 1, 1, S, >= T]
-    or None; max_kv_len = max(kv_lens).  Returns out [B, Hq, S, D] in q.dtype,
-    a view of a [B, S, Hq, D] buffer unless `out` is given.
+    or None; kv_starts int32 [B] or None (sequence b's rows see keys from
+    kv_starts[b] on: a left-padding mask as a key range); max_kv_len =
+    max(kv_lens).  Returns out [B, Hq, S, D] in q.dtype, a view of a
+    [B, S, Hq, D] buffer unless `out` is given.
     """
     if q.device.type != "cuda":
         raise HelmError("paged_prefill_attention runs on CUDA tensors only")
@@ -314,6 +317,9 @@ def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, page_table: tor
         raise HelmError("page_table and kv_lens must be int32")
     if page_table.stride(1) != 1:
         raise HelmError("page_table rows must be contiguous")
+    if kv_starts is not None and (kv_starts.dtype != torch.int32 or kv_starts.numel() != B
+                                  or not kv_starts.is_contiguous()):
+        raise HelmError("kv_starts must be a contiguous int32 tensor of one entry per sequence")
     dev = q.device
     if out is None:
         out = torch.empty(B, S, Hq, D, dtype=q.dtype, device=dev).transpose(1, 2)
@@ -337,7 +343,7 @@ def paged_prefill_attention(q: torch.Tensor, pool: torch.Tensor, page_table: tor
             q.data_ptr(), q.stride(0), q.stride(1), q.stride(2),
             pool.data_ptr(), pool.shape[0],
             page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
-            kv_lens.data_ptr(),
+            kv_lens.data_ptr(), None if kv_starts is None else kv_starts.data_ptr(),
             mask_ptr, mask_dt, mask_sb, mask_sq,
             out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
             ws.data_ptr(), ws_bytes,

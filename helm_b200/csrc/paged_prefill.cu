@@ -57,6 +57,7 @@ struct PrefillArgs {
   int64_t pt_sb;
   int max_pages;
   const int32_t* kv_lens;
+  const int32_t* kv_starts;  // optional [batch]: first key each sequence's rows may see
   const void* mask;
   int mask_dtype;
   int64_t mask_sb, mask_sq;
@@ -103,6 +104,15 @@ __device__ __forceinline__ int unit_keys(const PrefillArgs& a, int b, int rb, in
   return kv;
 }
 
+// First key the rows of sequence b may see: kv_starts[b] clamped to [0, kv_u]
+// (0 without kv_starts).  Keys before it are masked like keys past the causal
+// limit, and whole tiles before it are not visited, so HELM's left-padding
+// mask becomes a per-sequence key range instead of a mask read per element.
+__device__ __forceinline__ int unit_first_key(const PrefillArgs& a, int b, int kv_u) {
+  if (a.kv_starts == nullptr) return 0;
+  return min(max(a.kv_starts[b], 0), kv_u);
+}
+
 template <typename T>
 __device__ __forceinline__ float pf_mask(const PrefillArgs& a, int b, int s, int j) {
   const int64_t off = static_cast<int64_t>(b) * a.mask_sb + static_cast<int64_t>(s) * a.mask_sq + j;
@@ -132,9 +142,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const int pair = rest / a.splits;
   const int b = pair / a.hkv, h = pair - (pair / a.hkv) * a.hkv;
   const int kv_u = unit_keys(a, b, rb, kPfRows);
-  const int n_tiles = (kv_u + kPfTile - 1) / kPfTile;
-  const int t_begin = static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
-  const int t_end = static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
+  const int k_lo = unit_first_key(a, b, kv_u);
+  const int t_lo = k_lo / kPfTile;
+  const int n_tiles = (kv_u + kPfTile - 1) / kPfTile - t_lo;
+  const int t_begin = t_lo + static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
+  const int t_end = t_lo + static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
   const int n = t_end - t_begin;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -282,8 +294,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
           xA *= a.scale_log2;
           xB *= a.scale_log2;
         }
-        const bool inA = okA && c < vend && (!a.causal || jj <= posA);
-        const bool inB = okB && c < vend && (!a.causal || jj <= posB);
+        const bool inA = okA && c < vend && jj >= k_lo && (!a.causal || jj <= posA);
+        const bool inB = okB && c < vend && jj >= k_lo && (!a.causal || jj <= posB);
         if (a.mask != nullptr) {
           if (inA) xA += mask_log2(pf_mask<T>(a, b, sA, jj));
           if (inB) xB += mask_log2(pf_mask<T>(a, b, sB, jj));

@@ -258,9 +258,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const int pair = rest / a.splits;
   const int b = pair / a.hkv, h = pair - (pair / a.hkv) * a.hkv;
   const int kv_u = unit_keys(a, b, rb, kTcRows);
-  const int n_tiles = (kv_u + kTcTile - 1) / kTcTile;
-  const int t_begin = static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
-  const int t_end = static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
+  const int k_lo = unit_first_key(a, b, kv_u);
+  const int t_lo = k_lo / kTcTile;
+  const int n_tiles = (kv_u + kTcTile - 1) / kTcTile - t_lo;
+  const int t_begin = t_lo + static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
+  const int t_end = t_lo + static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
   const int n = t_end - t_begin;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -475,7 +477,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         x[c] = __uint_as_float(ra[c]);
         x[32 + c] = __uint_as_float(rb2[c]);
       }
-      const bool all_in = okr && vend >= kTcTile && (!a.causal || j0 + kTcTile - 1 <= pos);
+      const bool all_in = okr && vend >= kTcTile && j0 >= k_lo &&
+                          (!a.causal || j0 + kTcTile - 1 <= pos);
       if (a.softcap > 0.f) {
 #pragma unroll
         for (int c = 0; c < 64; ++c) x[c] = a.softcap * tanhf(x[c] * a.scale / a.softcap) * kLog2e;
@@ -488,7 +491,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       float mx = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        const bool in = all_in || (okr && c < vend && (!a.causal || j0 + c <= pos));
+        const bool in =
+            all_in || (okr && c < vend && j0 + c >= k_lo && (!a.causal || j0 + c <= pos));
         x[c] = in ? x[c] : -INFINITY;
         mx = fmaxf(mx, x[c]);
       }
@@ -682,9 +686,11 @@ __global__ void __launch_bounds__(kT2Threads, 1)
   const int pair = rest / a.splits;
   const int b = pair / a.hkv, h = pair - (pair / a.hkv) * a.hkv;
   const int kv_u = unit_keys(a, b, rb, kT2Rows);
-  const int n_tiles = (kv_u + kTcTile - 1) / kTcTile;
-  const int t_begin = static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
-  const int t_end = static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
+  const int k_lo = unit_first_key(a, b, kv_u);
+  const int t_lo = k_lo / kTcTile;
+  const int n_tiles = (kv_u + kTcTile - 1) / kTcTile - t_lo;
+  const int t_begin = t_lo + static_cast<int>(static_cast<int64_t>(n_tiles) * split / a.splits);
+  const int t_end = t_lo + static_cast<int>(static_cast<int64_t>(n_tiles) * (split + 1) / a.splits);
   const int n = t_end - t_begin;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -892,7 +898,8 @@ __global__ void __launch_bounds__(kT2Threads, 1)
         x[c] = __uint_as_float(ra[c]);
         x[32 + c] = __uint_as_float(rb2[c]);
       }
-      const bool all_in = okr && vend >= kTcTile && (!a.causal || j0 + kTcTile - 1 <= pos);
+      const bool all_in = okr && vend >= kTcTile && j0 >= k_lo &&
+                          (!a.causal || j0 + kTcTile - 1 <= pos);
       // Most tiles: every key of every row of the warp is visible, no mask and
       // no soft-cap.  Then the row max is taken on the raw scores (the scale is
       // positive, so the order and the rounded scaled max are the same) and
@@ -917,7 +924,8 @@ __global__ void __launch_bounds__(kT2Threads, 1)
           add_mask_row(a, b, s_pos, j0, all_in ? kTcTile : min(vend, kTcTile), x);
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const bool in = all_in || (okr && c < vend && (!a.causal || j0 + c <= pos));
+          const bool in =
+              all_in || (okr && c < vend && j0 + c >= k_lo && (!a.causal || j0 + c <= pos));
           x[c] = in ? x[c] : -INFINITY;
           mx = fmaxf(mx, x[c]);
         }
@@ -1223,8 +1231,9 @@ extern "C" int64_t helm_paged_prefill_workspace_bytes(int batch, int q_len, int 
 extern "C" int helm_paged_prefill_attention(
     const void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_s, const void* kv_pool,
     int64_t pool_pages, const int32_t* page_table, int64_t pt_stride_b, int max_pages,
-    const int32_t* kv_lens, const void* mask, int mask_dtype, int64_t mask_stride_b,
-    int64_t mask_stride_q, void* out, int64_t out_stride_b, int64_t out_stride_h,
+    const int32_t* kv_lens, const int32_t* kv_starts, const void* mask, int mask_dtype,
+    int64_t mask_stride_b, int64_t mask_stride_q, void* out, int64_t out_stride_b,
+    int64_t out_stride_h,
     int64_t out_stride_s, void* workspace, int64_t workspace_bytes, int batch, int q_len,
     int num_q_heads, int num_kv_heads, int head_dim, int page_size, int dtype, int causal,
     float scale, float softcap, int max_kv_len, void* stream) {
@@ -1266,6 +1275,7 @@ extern "C" int helm_paged_prefill_attention(
   a.pt_sb = pt_stride_b;
   a.max_pages = max_pages;
   a.kv_lens = kv_lens;
+  a.kv_starts = kv_starts;
   a.mask = mask;
   a.mask_dtype = mask_dtype;
   a.mask_sb = mask_stride_b;

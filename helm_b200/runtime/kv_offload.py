@@ -263,45 +263,56 @@ def _append_prefill_batched(kvcms, k, v, layer_idx: int) -> list:
     return past_lengths
 
 
-_CAUSAL_MEMO: list = []  # [(weakref to the caller's mask tensor, key, verdict)], newest last
+_CAUSAL_MEMO: list = []  # [(weakref to the caller's mask tensor, key, starts)], newest last
 
 
-def _is_chunk_causal(attention_mask: torch.Tensor, mask: torch.Tensor, lens: np.ndarray,
-                     S: int) -> bool:
-    """True when mask [B|1, 1, S, T] (a slice of attention_mask) is HELM's
-    chunk-causal mask without padding (pipeline_runtime.py:96-112): 0 where key
-    j <= lens[b] - S + i, and <= -1e4 everywhere else.  Every row then keeps
-    its own key, so the masked keys get weight exp(<= -1e4) = 0 in fp32 and
-    the kernel's causal limit gives the same result without reading the mask.
-    Decided once per mask tensor and lengths (one device reduction + sync):
-    the same mask object serves every layer of a chunk."""
+def _chunk_mask_starts(attention_mask: torch.Tensor, mask: torch.Tensor, lens: np.ndarray,
+                       S: int) -> Optional[np.ndarray]:
+    """The first visible key of each sequence when mask [B|1, 1, S, T] (a
+    slice of attention_mask) is HELM's chunk mask (pipeline_runtime.py:96-112)
+    with or without left key padding: 0 exactly where
+    starts[b] <= key j <= lens[b] - S + i, and <= -1e4 everywhere else, with
+    every row seeing at least one key.  Returns starts (int32, one entry per
+    mask row; all zero without padding), or None when the mask is anything
+    else.  The kernel then applies the causal limit and the key start itself
+    and reads no mask: the masked keys get weight exp(<= -1e4) = 0 in fp32
+    either way.  Decided once per mask tensor and lengths (one device
+    reduction + sync): the same mask object serves every layer of a chunk."""
     base = attention_mask._base if attention_mask._base is not None else attention_mask
     key = (tuple(mask.shape), tuple(mask.stride()), mask.storage_offset(), base._version,
            lens.tobytes(), S)
-    for ref, k, verdict in _CAUSAL_MEMO:
+    for ref, k, starts in _CAUSAL_MEMO:
         if ref() is base and k == key:
-            return verdict
+            return starts
     B, T = mask.shape[0], mask.shape[3]
-    verdict = False
+    starts = None
     if B == len(lens) or bool(np.all(lens == lens[0])):
         dev = mask.device
         past = torch.as_tensor(lens[:B].astype(np.int64) - S, device=dev).view(-1, 1, 1)
+        m = mask[:, 0]
+        # candidate start: the first visible key of the last row (the widest)
+        zero = m[:, S - 1, :] == 0
+        first = torch.where(zero.any(dim=1), zero.to(torch.int32).argmax(dim=1),
+                            torch.full((B,), T, dtype=torch.int64, device=dev))
         i = torch.arange(S, device=dev).view(1, S, 1)
         j = torch.arange(T, device=dev).view(1, 1, T)
-        allowed = j <= past + i
-        m = mask[:, 0]
-        verdict = bool(torch.where(allowed, m == 0, m <= -1e4).all())
-    _CAUSAL_MEMO.append((weakref.ref(base), key, verdict))
+        allowed = (j >= first.view(-1, 1, 1)) & (j <= past + i)
+        ok = torch.where(allowed, m == 0, m <= -1e4).all() & (first.view(-1) <= past.view(-1)).all()
+        res = torch.cat([ok.view(1).to(torch.int64), first.to(torch.int64)]).cpu().numpy()
+        if res[0]:
+            starts = res[1:].astype(np.int32)
+    _CAUSAL_MEMO.append((weakref.ref(base), key, starts))
     del _CAUSAL_MEMO[:-4]
-    return verdict
+    return starts
 
 
 def _kernel_prefill(q, pool, slots, kl, lens, T: int, P: int, scale: float, attention_mask,
                     mask, softcap):
     """helm_paged_prefill_attention when the chunk's mask lets the kernel serve
-    it: HELM's chunk-causal mask (recognised, then applied as the causal limit
-    without reading it), no mask, or a soft-cap (the mask read); None
-    otherwise (see _prefill_dense_pages for the environment switch)."""
+    it: HELM's chunk mask, with or without left key padding (recognised, then
+    applied as the causal limit and a per-sequence first key without reading
+    it), no mask, or a soft-cap (the mask read); None otherwise (see
+    _prefill_dense_pages for the environment switch)."""
     Hkv = pool.shape[2]
     native = (pool.dtype == q.dtype and _capi.prefill_supported(q.dtype, q.shape[-1], P)
               and (mask is None or (mask.dim() == 4 and mask.shape[1] == 1
@@ -309,16 +320,24 @@ def _kernel_prefill(q, pool, slots, kl, lens, T: int, P: int, scale: float, atte
                                     and mask.dtype in (torch.float32, torch.bfloat16,
                                                        torch.float16))))
     choice = os.environ.get("HELM_B200_NATIVE_PREFILL")
-    use_kernel = causal = False
+    use_kernel = False
+    starts = None
     if native and (choice != "0" or softcap is not None):
-        causal = mask is not None and _is_chunk_causal(attention_mask, mask, lens, q.shape[2])
-        use_kernel = softcap is not None or choice == "1" or mask is None or causal
+        if mask is not None:
+            starts = _chunk_mask_starts(attention_mask, mask, lens, q.shape[2])
+        use_kernel = softcap is not None or choice == "1" or mask is None or starts is not None
     if not use_kernel:
         return None
+    causal = starts is not None
+    kv_starts = None
+    if causal and starts.any():
+        B = q.shape[0]
+        kv_starts = torch.from_numpy(np.ascontiguousarray(
+            np.broadcast_to(starts, (B,)) if starts.size == 1 else starts)).to(q.device)
     return _capi.paged_prefill_attention(q, pool, slots, kl, num_kv_heads=Hkv, page_size=P,
                                          scale=scale, max_kv_len=T,
                                          mask=None if causal else mask, causal=causal,
-                                         softcap=softcap)
+                                         softcap=softcap, kv_starts=kv_starts)
 
 
 def _prefill_first_chunk(q, k, v, attention_mask, scale: float, softcap):
@@ -356,13 +375,15 @@ def _prefill_dense_pages(kvcms, q, layer_idx: int, scale: float,
     Two device paths, both with HELM's additive mask (chunk-causal + padding,
     kv_offload.py:206-227):
       * helm_paged_prefill_attention, reading K/V in place from the pool (no
-        dense copy; tcgen05 kernel): used when the mask is HELM's chunk-causal
-        mask (recognised once per mask, then applied as the kernel's causal
-        limit without reading it), when there is no mask, and for soft-capped
+        dense copy; tcgen05 kernel): used when the mask is HELM's chunk mask
+        with or without left key padding (recognised once per mask, then
+        applied as the kernel's causal limit and per-sequence first key
+        without reading it), when there is no mask, and for soft-capped
         scores;
       * K/V gathered to dense [B, Hkv, T, D] by one gather_kv launch, then one
-        library attention (torch SDPA): used for other masks (key padding),
-        which the kernel would read element by element.
+        library attention (torch SDPA): used for other masks (arbitrary
+        patterns, or padding that leaves a query row without any key), which
+        the kernel would read element by element.
     HELM_B200_NATIVE_PREFILL=1 sends every chunk to the kernel, =0 every chunk
     without softcap to the library.  The kernel needs bf16/fp16, head dim 64
     or 128 and a page size that is a multiple of 16.  None when the page lists

@@ -233,6 +233,11 @@ int helm_gather_kv(const void* kv_pool, int64_t pool_pages, const int32_t* page_
  *  q           [B, Hq, q_len, D] with strides q_stride_b/_h/_s (elements; even)
  *  kv_pool     [pool_pages, 2, Hkv, page_size, D]; page_size a multiple of 16
  *  page_table  int32 [B, >= max_pages] (row stride pt_stride_b), kv_lens int32 [B]
+ *  kv_starts   optional int32 [B]: key j is visible to sequence b's rows only if
+ *              j >= kv_starts[b].  HELM's key-padding mask of a left-padded
+ *              prompt (helm/runtime/pipeline_runtime.py:107-111) passed as a
+ *              key range: the padded keys' tiles are skipped and no mask is
+ *              read.  NULL: every key from 0.
  *  mask        optional additive mask [B or 1, 1, q_len, >= max kv_lens] with
  *              strides mask_stride_b (0 to broadcast) and mask_stride_q, last
  *              stride 1; fp32, bf16 or fp16
@@ -254,10 +259,11 @@ int64_t helm_paged_prefill_workspace_bytes(int batch, int q_len, int num_q_heads
 int helm_paged_prefill_attention(const void* q, int64_t q_stride_b, int64_t q_stride_h,
                                  int64_t q_stride_s, const void* kv_pool, int64_t pool_pages,
                                  const int32_t* page_table, int64_t pt_stride_b, int max_pages,
-                                 const int32_t* kv_lens, const void* mask, int mask_dtype,
-                                 int64_t mask_stride_b, int64_t mask_stride_q, void* out,
-                                 int64_t out_stride_b, int64_t out_stride_h, int64_t out_stride_s,
-                                 void* workspace, int64_t workspace_bytes, int batch, int q_len,
+                                 const int32_t* kv_lens, const int32_t* kv_starts,
+                                 const void* mask, int mask_dtype, int64_t mask_stride_b,
+                                 int64_t mask_stride_q, void* out, int64_t out_stride_b,
+                                 int64_t out_stride_h, int64_t out_stride_s, void* workspace,
+                                 int64_t workspace_bytes, int batch, int q_len,
                                  int num_q_heads, int num_kv_heads, int head_dim, int page_size,
                                  int dtype, int causal, float scale, float softcap, int max_kv_len,
                                  void* stream);

@@ -33,7 +33,8 @@ def _prefill(**kw):
     a.update(kw)
     return _capi.lib().helm_paged_prefill_attention(
         a["q"], a["q_sb"], a["q_sh"], a["q_ss"], a["pool"], a["pool_pages"], a["pt"], a["pt_sb"],
-        a["max_pages"], a["lens"], a["mask"], a["mask_dtype"], a["mask_sb"], a["mask_sq"],
+        a["max_pages"], a["lens"], None, a["mask"], a["mask_dtype"], a["mask_sb"],
+        a["mask_sq"],
         a["out"], a["o_sb"], a["o_sh"], a["o_ss"], a["ws"], a["ws_bytes"], a["batch"], a["S"],
         a["hq"], a["hkv"], a["d"], a["page"], a["dtype"], a["causal"], 0.088, 0.0, 300, None)
 

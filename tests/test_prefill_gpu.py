@@ -150,6 +150,43 @@ def test_prefill_rows_without_keys_are_zero(kernel):
     assert err.max() <= 1e-2 + 1e-2 * float(np.abs(ref).max())
 
 
+PAD_CASES = [
+    # dtype, Hq, Hkv, D, P, lens, S, left pads per sequence
+    (torch.bfloat16, 8, 2, 128, 16, [700, 900, 333], 100, [70, 0, 200]),
+    (torch.float16, 8, 8, 64, 64, [520, 515], 129, [64, 3]),
+    (torch.bfloat16, 40, 8, 128, 64, [4096], 16, [1000]),   # split key range, empty splits
+]
+
+
+@pytest.mark.parametrize("case", PAD_CASES, ids=[f"pad{i}" for i in range(len(PAD_CASES))])
+def test_prefill_key_starts_match_padding_mask(case, kernel):
+    """HELM's chunk mask of a left-padded batch (causal + key padding,
+    pipeline_runtime.py:96-112) given as causal=True and kv_starts = the pad
+    lengths, with no mask read: the oracle with the full additive mask, and the
+    kernel reading that mask, agree with it.  Starts fall inside tiles, on tile
+    edges and at 0."""
+    dev = _cuda()
+    dtype, Hq, Hkv, D, P, lens, S, pads = case
+    B, T = len(lens), max(lens)
+    pool, perm, q, _ = _setup(dev, dtype, B, Hq, Hkv, D, P, lens, S, seed=sum(pads) + S)
+    mask = _chunk_mask(lens, S, dtype, pad={b: p for b, p in enumerate(pads) if p})
+    scale = D ** -0.5
+    args = (q.to(dev), pool.to(dev), perm.to(dev),
+            torch.tensor(lens, dtype=torch.int32, device=dev))
+    kw = dict(num_kv_heads=Hkv, page_size=P, scale=scale, max_kv_len=T)
+    got = _capi.paged_prefill_attention(
+        *args, causal=True, kv_starts=torch.tensor(pads, dtype=torch.int32, device=dev), **kw)
+    read = _capi.paged_prefill_attention(*args, mask=mask.to(dev), **kw)
+    torch.cuda.synchronize()
+    assert _capi.device_status(dev) == 0
+    ref = _oracle(pool, perm, q, lens, P, Hkv, mask, False, 0.0, scale)
+    g, r = got.float().cpu().numpy(), read.float().cpu().numpy()
+    assert np.isfinite(g).all()
+    atol, rtol = TOL[dtype]
+    assert (np.abs(g - ref) <= atol + rtol * np.abs(ref)).all(), np.abs(g - ref).max()
+    assert (np.abs(g - r) <= atol + rtol * np.abs(r)).all(), np.abs(g - r).max()
+
+
 def test_prefill_output_layout_and_arguments(kernel):
     """The default output is a [B, Hq, S, D] view of a [B, S, Hq, D] buffer
     (what the attention forward reshapes next); a strided caller buffer is

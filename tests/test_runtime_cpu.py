@@ -372,24 +372,36 @@ def test_host_tier_placement_matches_reference(placement_golden):
 
 
 def test_chunk_causal_mask_detection():
-    """HELM's chunk-prefill mask without padding (pipeline_runtime.py:96-112)
-    is recognised as the causal limit (the native kernel then reads no mask);
-    padding, a visible future key or other lengths are not."""
+    """HELM's chunk-prefill mask (pipeline_runtime.py:96-112) is recognised as
+    the causal limit plus a first visible key per sequence (the native kernel
+    then reads no mask): without padding the starts are 0, with left key
+    padding they are the padded lengths.  A visible future key, other lengths,
+    padding with a hole, or padding that leaves a row without any key are not
+    recognised."""
     import numpy as np
-    from helm_b200.runtime.kv_offload import _is_chunk_causal
+    from helm_b200.runtime.kv_offload import _chunk_mask_starts
     S, T = 6, 20
     i = torch.arange(S).view(S, 1)
     j = torch.arange(T).view(1, T)
     for dtype in (torch.bfloat16, torch.float16, torch.float32):
         mn = torch.finfo(dtype).min
         m = torch.where(j <= T - S + i, 0.0, mn).to(dtype).view(1, 1, S, T)
-        assert _is_chunk_causal(m, m, np.array([T], np.int32), S)
+        assert _chunk_mask_starts(m, m, np.array([T], np.int32), S).tolist() == [0]
         two = m.expand(2, 1, S, T)
-        assert _is_chunk_causal(two, two, np.array([T, T], np.int32), S)
-        padded = m.clone()
-        padded[0, 0, :, :3] = mn
-        assert not _is_chunk_causal(padded, padded, np.array([T], np.int32), S)
+        assert _chunk_mask_starts(two, two, np.array([T, T], np.int32), S).tolist() == [0, 0]
+        # HELM adds the key padding to the causal mask (min + min = -inf there)
+        pads = torch.tensor([3, 0, 14])
+        keep = (j >= pads.view(3, 1, 1)).to(dtype)
+        padded = (m + ((1.0 - keep) * mn).view(3, 1, 1, T)).to(dtype)
+        got = _chunk_mask_starts(padded, padded, np.array([T, T, T], np.int32), S)
+        assert got is not None and got.tolist() == [3, 0, 14]
+        lone = padded.clone()
+        lone[2, 0, :, :15] = mn      # row 0 of sequence 2 sees no key
+        assert _chunk_mask_starts(lone, lone, np.array([T, T, T], np.int32), S) is None
+        hole = padded.clone()
+        hole[1, 0, :, 5] = mn        # a masked key after a visible one
+        assert _chunk_mask_starts(hole, hole, np.array([T, T, T], np.int32), S) is None
         future = m.clone()
         future[0, 0, 0, T - 1] = 0
-        assert not _is_chunk_causal(future, future, np.array([T], np.int32), S)
-        assert not _is_chunk_causal(m, m, np.array([T - 1], np.int32), S)
+        assert _chunk_mask_starts(future, future, np.array([T], np.int32), S) is None
+        assert _chunk_mask_starts(m, m, np.array([T - 1], np.int32), S) is None

@@ -266,6 +266,46 @@ def test_dense_prefill_path_matches_page_walk(dev, monkeypatch, native):
                 assert fast is None
 
 
+def test_dense_prefill_padding_mask_runs_on_the_kernel(dev, monkeypatch):
+    """A later prefill chunk of a left-padded batch (HELM's chunk mask plus key
+    padding, pipeline_runtime.py:96-112) runs on the native kernel with the
+    padding as per-sequence first keys (gather + library attention is not
+    called) and equals the fp32 page walk within the bf16 tolerance; a mask
+    that leaves a query row without any key still takes the library path."""
+    from helm_b200 import _capi
+    from helm_b200.runtime.kv_cache import _prefill_over_pages
+    from helm_b200.runtime.kv_offload import _prefill_dense_pages
+    monkeypatch.delenv("HELM_B200_NATIVE_PREFILL", raising=False)
+    torch.manual_seed(12)
+    H, D, P, T, S = 2, 128, 16, 400, 96
+    pads = [37, 0, 150]
+    alloc = KVAllocator(1, H, D, page_size=P, dtype=torch.bfloat16)
+    mgrs = []
+    for _ in pads:
+        m = KVCacheManager(alloc, gpu_high_watermark_bytes=10 ** 12)
+        m.append_prefill(0, torch.randn(1, H, T, D).to(torch.bfloat16).to(dev),
+                         torch.randn(1, H, T, D).to(torch.bfloat16).to(dev))
+        mgrs.append(m)
+    q = torch.randn(len(pads), 4 * H, S, D).to(torch.bfloat16).to(dev)
+    mn = torch.finfo(torch.bfloat16).min
+    i = torch.arange(S, device=dev).view(S, 1)
+    j = torch.arange(T, device=dev).view(1, T)
+    causal = torch.where(j <= T - S + i, 0.0, mn)
+    keep = (j.view(1, T) >= torch.tensor(pads, device=dev).view(-1, 1)).float()
+    mask = (causal.view(1, 1, S, T) + ((1.0 - keep) * mn).view(-1, 1, 1, T)).to(torch.bfloat16)
+    calls = []
+    real_gather = _capi.gather_kv
+    monkeypatch.setattr(_capi, "gather_kv", lambda *a, **k: calls.append(1) or real_gather(*a, **k))
+    fast = _prefill_dense_pages(mgrs, q, 0, D ** -0.5, mask)
+    assert fast is not None and not calls
+    ref = _prefill_over_pages(q, [m.iterate_layer_pages(0) for m in mgrs], D ** -0.5, mask, None)
+    _close(fast, ref, torch.bfloat16)
+    lone = mask.clone()
+    lone[2, 0, 0, :] = mn       # query row 0 of sequence 2 sees no key: library path
+    _prefill_dense_pages(mgrs, q, 0, D ** -0.5, lone)
+    assert calls
+
+
 def test_gemma2_sliding_window_known_answers(dev):
     """The reference's analytic check of the Gemma-2 forward
     (tests/unit/runtime/test_kv_offload.py:367-413), restated at a head size the
