@@ -74,13 +74,19 @@ size_t gemv_smem_bytes(int64_t k, bool norm) {
 
 constexpr int kArMaxRanks = 8;
 // Exchange buffer: header {uint32 call epoch, uint32 CTAs done} (padded to
-// 256 bytes), then words {fp32 value, epoch} [2 parities][world][n][kArBatch].
+// 256 bytes), then words {fp32 value, epoch} [2 parities][world][kArBatch][n].
 // The epoch belongs to the call, not to a CTA, and the batch stride is fixed:
 // consecutive calls with different grids or batch slices then use disjoint
 // parity halves for every (row, batch row) word, so a rank one call ahead
-// never overwrites a word a slower rank has still to read.
+// never overwrites a word a slower rank has still to read.  Every call on one
+// buffer has the same n (the buffer is sized for it; the tensor-parallel
+// projections that all-reduce all produce the hidden size).
 constexpr int64_t kArHeaderBytes = 256;
 constexpr int kArBatch = 16;  // the widest batch one call takes
+// rows one CTA of the CUDA-core form owns in an all-reduce call (a contiguous
+// range; their partials are staged in shared memory, pushed group by group as
+// coalesced writes, and summed after the loop)
+constexpr int kArCtaRows = 256;
 
 struct GemvArgs {
   unsigned char* bufs[kArMaxRanks];  // all-reduce exchange buffers of every rank
@@ -171,33 +177,37 @@ __device__ __forceinline__ uint64_t gemv_timer_ns() {
   return t;
 }
 
-// All-reduce of one output value over the ranks (tensor-parallel row-parallel
-// projection).  Words {fp32 value, epoch} [2 parities][world][n][batch] in
-// every rank's buffer.  ar_push stores this rank's partial for (row, b) into
-// slot `rank` of every buffer (NVLink stores, no wait); ar_poll later reads
-// all ranks' partials of (row, b) from this rank's buffer and returns their
-// sum in rank order (the same on every rank), or false when the poll ran out
-// of time (status word set).  Pushing every row first and polling afterwards
-// costs one NVLink round trip per call instead of one per row group.
+// All-reduce of the output values over the ranks (tensor-parallel
+// row-parallel projection).  Words {fp32 value, epoch} in every rank's buffer,
+// laid out [2 parities][world][kArBatch][n]: the words of consecutive rows of
+// one batch row are consecutive, so the rows a CTA owns go to a peer as a few
+// coalesced NVLink writes instead of one 8-byte write each (at 8 ranks the
+// per-word form spent most of its time on the links' small-write rate).
+// ar_word: the word of (source rank slot, batch row b, row) in buffer buf.
+__device__ __forceinline__ uint2* ar_word(const GemvArgs& a, unsigned char* buf, int par,
+                                          int slot, int b, int64_t row) {
+  return reinterpret_cast<uint2*>(buf + kArHeaderBytes) +
+         ((static_cast<int64_t>(par) * a.world + slot) * kArBatch + b) * a.n + row;
+}
+
+// ar_push stores this rank's partial for (row, b) into slot `rank` of every
+// buffer (NVLink stores, no wait); ar_poll later reads all ranks' partials of
+// (row, b) from this rank's buffer and returns their sum in rank order (the
+// same on every rank), or false when the poll ran out of time (status word
+// set).  Pushing every row first and polling afterwards costs one NVLink round
+// trip per call instead of one per row group.
 __device__ __forceinline__ void ar_push(const GemvArgs& a, uint32_t e, int64_t row, int b,
                                         float part) {
   const int par = static_cast<int>(e & 1u);
-  const int64_t slot_words = a.n * kArBatch;
-  const int64_t off = row * kArBatch + b;
-  for (int p = 0; p < a.world; ++p) {
-    uint2* dst = reinterpret_cast<uint2*>(a.bufs[p] + kArHeaderBytes) +
-                 (static_cast<int64_t>(par) * a.world + a.rank) * slot_words + off;
-    st_volatile_u2(dst, __float_as_uint(part), e);
-  }
+  for (int p = 0; p < a.world; ++p)
+    st_volatile_u2(ar_word(a, a.bufs[p], par, a.rank, b, row), __float_as_uint(part), e);
 }
 
 __device__ __forceinline__ bool ar_poll(const GemvArgs& a, uint32_t e, int64_t row, int b,
                                         uint64_t t0, float& sum) {
   const int par = static_cast<int>(e & 1u);
-  const int64_t slot_words = a.n * kArBatch;
-  const int64_t off = row * kArBatch + b;
-  const uint2* own = reinterpret_cast<const uint2*>(a.bufs[a.rank] + kArHeaderBytes) +
-                     static_cast<int64_t>(par) * a.world * slot_words + off;
+  const int64_t slot_words = static_cast<int64_t>(kArBatch) * a.n;
+  const uint2* own = ar_word(a, a.bufs[a.rank], par, 0, b, row);
   uint2 w[kArMaxRanks];
   for (int spin = 0;; ++spin) {
     bool ready = true;
@@ -637,10 +647,26 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, GemvShape<NB>::kMinBl
   const int64_t cs = (chunks + ksplit - 1) / ksplit;
   const int64_t c_begin = ws * cs, c_end = min(chunks, c_begin + cs);
   const int nj = static_cast<int>((cs + 32 * kU - 1) / (32 * kU));  // items per row
-  const int64_t first = static_cast<int64_t>(blockIdx.x) * rpi;
-  const int64_t gstride = static_cast<int64_t>(gridDim.x) * rpi;
-  const int n_groups = first < a.n ? static_cast<int>((a.n - first + gstride - 1) / gstride) : 0;
+  // row groups of this CTA: strided over the grid, or (all-reduce) one
+  // contiguous range, so that its rows' words are contiguous in the exchange
+  // buffers (groups shared out evenly, one more or less per CTA)
+  int64_t first, gstride;
+  int n_groups;
+  if (AR) {
+    const int64_t groups = (a.n + rpi - 1) / rpi;
+    const int64_t g0 = groups * blockIdx.x / gridDim.x;
+    const int64_t g1 = groups * (blockIdx.x + 1) / gridDim.x;
+    first = g0 * rpi;
+    gstride = rpi;
+    n_groups = static_cast<int>(g1 - g0);
+  } else {
+    first = static_cast<int64_t>(blockIdx.x) * rpi;
+    gstride = static_cast<int64_t>(gridDim.x) * rpi;
+    n_groups = first < a.n ? static_cast<int>((a.n - first + gstride - 1) / gstride) : 0;
+  }
   const int total = n_groups * nj;
+  // all-reduce: this CTA's partials, [row - first][batch row], pushed together
+  __shared__ float s_ar[AR ? kArCtaRows : 1][NB];
   auto slot_addr = [&](int r, int stream, int u) -> uint32_t {
     return ring + static_cast<uint32_t>((((r * kStreams + stream) * kU + u) * kGemvThreads +
                                          threadIdx.x) * 16);
@@ -760,33 +786,45 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, GemvShape<NB>::kMinBl
       for (int b = 0; b < NB; ++b) {
         if (lane != b || b >= a.batch) continue;
         if (AR)
-          ar_push(a, s_epoch, row, b, acc[b]);  // summed and emitted after the loop
+          s_ar[row - first][b] = acc[b];  // pushed below, summed and emitted after the loop
         else
           emit_value<T, GLU>(a, row, b, acc[b], acc2[b]);
+      }
+    }
+    if (AR) {
+      // push the group's rows to every rank now, while the next group streams:
+      // word (this rank, b, row), consecutive threads on consecutive rows, so
+      // the group's rows of one batch row leave as one contiguous write
+      __syncthreads();
+      const int64_t g0 = first + static_cast<int64_t>(g - 1) * gstride;
+      const int grows = static_cast<int>(min(a.n, g0 + rpi) - g0);
+      const int items = a.world * a.batch * grows;
+      for (int it = threadIdx.x; it < items; it += kGemvThreads) {
+        const int r = it % grows, pb = it / grows;
+        const int b = pb % a.batch, p = pb / a.batch;
+        st_volatile_u2(ar_word(a, a.bufs[p], static_cast<int>(s_epoch & 1u), a.rank, b, g0 + r),
+                       __float_as_uint(s_ar[g0 + r - first][b]), s_epoch);
       }
     }
 #pragma unroll
     for (int b = 0; b < NB; ++b) acc[b] = acc2[b] = 0.f;
   }
   cp_async_wait<0>();
-  if (AR && ws == 0) {  // every partial is out: sum the ranks', emit
-    // the warp's (row group, batch row) values spread over its lanes, so the
-    // polls of different rows run concurrently
+  if (AR) {
+    const int rows = static_cast<int>(min(a.n, first + static_cast<int64_t>(n_groups) * rpi) - first);
+    // every row of this CTA is pushed: poll this rank's buffer for every
+    // rank's words of our rows, sum in rank order, emit (consecutive threads,
+    // consecutive rows)
     const uint64_t t0 = gemv_timer_ns();
-    const int items = n_groups * a.batch;
-    for (int it = lane; it < items; it += 32) {
-      const int g2 = it / a.batch, b = it - (it / a.batch) * a.batch;
-      const int64_t row = first + g2 * gstride + wrow;
-      if (row >= a.n) continue;
+    for (int it = threadIdx.x; it < a.batch * max(rows, 0); it += kGemvThreads) {
+      const int r = it % rows, b = it / rows;
       float sum = 0.f;
-      if (!ar_poll(a, s_epoch, row, b, t0, sum)) {
+      if (!ar_poll(a, s_epoch, first + r, b, t0, sum)) {
         atomicExch(&s_ar_ok, 0);
         break;
       }
-      emit_value<T, GLU>(a, row, b, sum, 0.f);
+      emit_value<T, GLU>(a, first + r, b, sum, 0.f);
     }
-  }
-  if (AR) {
     __syncthreads();
     if (threadIdx.x == 0) ar_finish_call(a, s_epoch);
   }
@@ -851,6 +889,8 @@ int launch_gemv(const GemvArgs& a, cudaStream_t stream) {
   const int64_t want = (a.n + rpi - 1) / rpi;
   const int grid = static_cast<int>(std::min<int64_t>(want, int64_t(num_sms_current_device()) * fit));
   if (AR && a.batch > kArBatch) return HELM_ERR_UNSUPPORTED;
+  // CUDA-core all-reduce: a CTA's contiguous rows are staged in shared memory
+  if (AR && !kMma && (want + grid - 1) / grid * rpi > kArCtaRows) return HELM_ERR_UNSUPPORTED;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(GemvShape<NB>::kThreads);
