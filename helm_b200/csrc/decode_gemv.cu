@@ -420,8 +420,6 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, 1) decode_gemv_kernel
   __shared__ float s_part[kGemvWarps][16][NB][kStreams];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, tq = lane & 3;
-  const T* x = static_cast<const T*>(a.x);
-  const T* nw = static_cast<const T*>(a.norm_w);
   const T* W = static_cast<const T*>(a.w);
   const T* W2 = static_cast<const T*>(a.w2);
   const int64_t ksteps = K / 16;
@@ -635,8 +633,6 @@ __global__ void __launch_bounds__(GemvShape<NB>::kThreads, GemvShape<NB>::kMinBl
   __shared__ float s_scale;
   __shared__ float s_part[kGemvWarps][NB][2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const T* x = static_cast<const T*>(a.x);
-  const T* nw = static_cast<const T*>(a.norm_w);
   const T* W = static_cast<const T*>(a.w);
   const T* W2 = static_cast<const T*>(a.w2);
   const int64_t chunks = K / 8;  // 16-byte chunks per row
